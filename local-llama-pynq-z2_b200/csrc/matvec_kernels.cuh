@@ -1,0 +1,279 @@
+// sm_100a kernels for the group-quantized matrix-vector product of the reference's hot path.
+//
+// Arithmetic contract (bit-exact with the reference C path):
+//   qwen/qwen.c:436-456 (matmul_cpu, fpga_matvec4's twin) and runq/runq.c:430-458 (matmul, fpga_matvec's twin):
+//     isum_g = sum_{k<gs} w[i, g*gs + k] * xq[g*gs + k]           int32, exact
+//     p_g    = ((float)isum_g * wscale[i, g]) * xs[g]             two fp32 multiplies, each rounded (no FMA)
+//     out[i] = (((0 + p_0) + p_1) + ...) + p_{ng-1}               fp32 adds in group order
+// The HLS kernels (hls4/matvec4.cpp:128-151, hls/matvec.cpp:320-344) compute the same sum; the int4 one adds
+// in a tree order, which the reference checks with a tolerance. Here the order is always the sequential one.
+//
+// Work decomposition: a CTA owns a tile of `rt` consecutive rows. Because rows are contiguous in the weight
+// plane, the tile's groups form one contiguous byte range, so the CTA streams flat group index u = r*ng + g
+// with 128-bit coalesced loads whatever ng is. Each thread turns one group into its product p (dp4a int
+// sums, fp16/fp32 scale), stores it to shared memory at [r][g], and after a barrier thread r adds row r's
+// products in group order. The activations are staged once per CTA in shared memory, in "planes" of
+// 16-byte chunks so that every warp-wide 128-bit shared load is conflict-free.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mvb {
+
+enum WeightFormat : int {
+    kQ4F16 = 0,  // .qwb int4 plane + fp16 scales (fpga_matvec4 wbits=4)
+    kQ8F16 = 1,  // .qwb int8 plane + fp16 scales (fpga_matvec4 wbits=8, the qwen head)
+    kQ8F32 = 2,  // runq int8 plane + fp32 scales (fpga_matvec, gs 32 or 64)
+};
+
+// How the activations reach the kernel.
+enum XMode : int {
+    kXQuantized = 0,   // xq (int8) and xs (fp32) given
+    kXQuantizeQwen = 1,  // fp32 x given; quantized in the prologue exactly like qwen.c:355-364
+    kXQuantizeRunq = 2,  // fp32 x given; quantized in the prologue exactly like runq.c:244-270
+};
+
+constexpr int kThreads = 256;
+constexpr int kMaxN = 8192;  // MAX_N of driver/matvec_fpga.cpp:70
+
+struct MatvecParams {
+    const uint8_t *w;   // weight plane, row-major, d rows of n*bits/8 bytes
+    const void *ws;     // weight scales: d * n/gs, fp16 bits or fp32
+    const int8_t *xq;   // n int8 activations (kXQuantized)
+    const float *xs;    // n/gs fp32 activation scales (kXQuantized)
+    const float *x;     // n fp32 activations (kXQuantize*)
+    float *out;         // d fp32 results
+    int n, d, rt;       // columns, rows, rows per CTA tile
+    int xmode;
+};
+
+// fp16 bits -> fp32 with qwen.c's semantics (qwen.c:84-94): exact for zero, subnormals and normals, and
+// exponent field 31 is a finite exponent (2^16), not inf/nan. Normal values are a pure rebias of the bit
+// pattern; subnormals are m * 2^-24, which fp32 holds exactly.
+__device__ __forceinline__ float scale_from_f16(uint32_t h) {
+    const uint32_t mag = h & 0x7FFFu;
+    const uint32_t bits = mag < 0x400u ? __float_as_uint(__fmul_rn(__uint2float_rn(mag), 5.9604644775390625e-08f))
+                                       : (mag << 13) + 0x38000000u;
+    return __uint_as_float(bits | ((h & 0x8000u) << 16));
+}
+
+// Streaming 128-bit load of weight bytes: read once, so keep them out of L1.
+__device__ __forceinline__ uint4 ld_weights(const void *p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_u16(const void *p) {
+    unsigned short v;
+    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float ld_f32(const void *p) {
+    float v;
+    asm("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+// Programmatic dependent launch: a no-op unless the launch carries the programmatic-serialization attribute.
+__device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_consumer() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Shared-memory layout of one CTA, for n columns, group size GS and tile rt:
+//   xplane[XC][ng] uint4   activation bytes, chunk c of group g at plane c (int4: even/odd element planes)
+//   xs[ng] fp32, xsum[ng] int32 (sum of a group's 32 activations, for the int4 offset correction)
+//   prod[rt][ng + 1] fp32  per-group products; the +1 keeps column reads of the fold conflict-free
+__host__ __device__ inline size_t matvec_smem_bytes(int n, int gs, int rt) {
+    const int ng = n / gs;
+    return (size_t)(gs / 16) * ng * 16 + (size_t)ng * 8 + (size_t)rt * (ng + 1) * 4;
+}
+
+// float -> int8 as the reference's casts behave on x86-64 (qwen.c:362, runq.c:266): NaN and values outside
+// int32 become INT32_MIN, whose low byte is 0; other values are truncated to 8 bits. Reached only by groups whose
+// scale is zero or subnormal (0/0, or 1/scale overflowing to inf); a plain device cast would saturate instead.
+__device__ __forceinline__ int8_t to_int8_x86(float r) {
+    return fabsf(r) < 2147483648.0f ? (int8_t)(int32_t)r : (int8_t)0;
+}
+
+// Quantizes group g of x into 32 (or 64) int8 values and one scale, as qwen.c:355-364 (kXQuantizeQwen) or
+// runq.c:244-270 (kXQuantizeRunq) do; writes the values to q (registers) and returns the scale.
+template <int GS>
+__device__ __forceinline__ float quantize_group(const float *x, int g, int mode, int8_t (&q)[GS]) {
+    float v[GS];
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)g * GS);
+#pragma unroll
+    for (int i = 0; i < GS / 4; i++) {
+        const float4 f = src[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < GS; i++) amax = fmaxf(amax, fabsf(v[i]));
+    float scale;
+    if (mode == kXQuantizeQwen) {
+        scale = __fmul_rn(amax, 1.0f / 127.0f);
+        const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < GS; i++) q[i] = to_int8_x86(roundf(__fmul_rn(v[i], inv)));
+    } else {
+        scale = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+        for (int i = 0; i < GS; i++) q[i] = to_int8_x86(roundf(__fdiv_rn(v[i], scale)));
+    }
+    return scale;
+}
+
+template <int FMT, int GS>
+__global__ void __launch_bounds__(kThreads) matvec_kernel(const MatvecParams p) {
+    constexpr int GB = FMT == kQ4F16 ? GS / 2 : GS;  // weight bytes per group
+    constexpr int WC = GB / 16;                        // 16-byte weight chunks per group
+    constexpr int XC = GS / 16;                        // 16-byte activation chunks per group
+    constexpr int K = FMT == kQ4F16 ? 4 : (GS == 32 ? 2 : 1);  // groups in flight per thread
+    extern __shared__ __align__(16) uint8_t smem[];
+
+    const int n = p.n, ng = n / GS;
+    const int row0 = blockIdx.x * p.rt;
+    const int rows = min(p.rt, p.d - row0);
+    uint4 *xplane = reinterpret_cast<uint4 *>(smem);
+    float *xs_s = reinterpret_cast<float *>(xplane + XC * ng);
+    int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
+    float *prod = reinterpret_cast<float *>(xsum_s + ng);
+    const int tid = threadIdx.x;
+
+    // The activations may come from the kernel launched just before this one.
+    wait_for_producer();
+
+    // Stage the activations in shared memory.
+    if (p.xmode == kXQuantized) {
+        for (int c = tid; c < n / 16; c += kThreads) {
+            const uint4 a = *reinterpret_cast<const uint4 *>(p.xq + 16 * c);
+            const int g = c / XC, k = c % XC;
+            if (FMT == kQ4F16) {
+                // chunk k of a group holds elements 16k..16k+15: words 2k, 2k+1 of the even (plane 0) and odd
+                // (plane 1) element planes; weight word j pairs its low nibbles with even word j, high with odd.
+                uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
+                uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
+                ev[0] = __byte_perm(a.x, a.y, 0x6420);
+                ev[1] = __byte_perm(a.z, a.w, 0x6420);
+                od[0] = __byte_perm(a.x, a.y, 0x7531);
+                od[1] = __byte_perm(a.z, a.w, 0x7531);
+            } else {
+                xplane[k * ng + g] = a;
+            }
+        }
+        for (int g = tid; g < ng; g += kThreads) xs_s[g] = p.xs[g];
+    } else {
+        for (int g = tid; g < ng; g += kThreads) {
+            int8_t q[GS];
+            xs_s[g] = quantize_group<GS>(p.x, g, p.xmode, q);
+            uint32_t wv[GS / 4];
+#pragma unroll
+            for (int j = 0; j < GS / 4; j++)
+                wv[j] = (uint32_t)(uint8_t)q[4 * j] | (uint32_t)(uint8_t)q[4 * j + 1] << 8 |
+                        (uint32_t)(uint8_t)q[4 * j + 2] << 16 | (uint32_t)(uint8_t)q[4 * j + 3] << 24;
+#pragma unroll
+            for (int k = 0; k < XC; k++) {
+                uint4 a = make_uint4(wv[4 * k], wv[4 * k + 1], wv[4 * k + 2], wv[4 * k + 3]);
+                if (FMT == kQ4F16) {
+                    uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
+                    uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
+                    ev[0] = __byte_perm(a.x, a.y, 0x6420);
+                    ev[1] = __byte_perm(a.z, a.w, 0x6420);
+                    od[0] = __byte_perm(a.x, a.y, 0x7531);
+                    od[1] = __byte_perm(a.z, a.w, 0x7531);
+                } else {
+                    xplane[k * ng + g] = a;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (FMT == kQ4F16) {
+        for (int g = tid; g < ng; g += kThreads) {
+            const uint4 e = xplane[g], o = xplane[ng + g];
+            int s = __dp4a((int)e.x, 0x01010101, 0);
+            s = __dp4a((int)e.y, 0x01010101, s);
+            s = __dp4a((int)e.z, 0x01010101, s);
+            s = __dp4a((int)e.w, 0x01010101, s);
+            s = __dp4a((int)o.x, 0x01010101, s);
+            s = __dp4a((int)o.y, 0x01010101, s);
+            s = __dp4a((int)o.z, 0x01010101, s);
+            s = __dp4a((int)o.w, 0x01010101, s);
+            xsum_s[g] = s;
+        }
+        __syncthreads();
+    }
+
+    // Stream this tile's groups: unit u = r*ng + g, contiguous in memory.
+    const int units = rows * ng;
+    const uint8_t *wt = p.w + (size_t)row0 * ng * GB;
+    const size_t s0 = (size_t)row0 * ng;
+    int r = tid / ng, g = tid % ng;
+    const int dr = kThreads / ng, dg = kThreads % ng;
+    for (int base = tid; base < units; base += K * kThreads) {
+        uint4 wv[K][WC];
+        float wsc[K];
+        uint32_t hs[K];
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int u = base + k * kThreads;
+            if (u < units) {
+#pragma unroll
+                for (int c = 0; c < WC; c++) wv[k][c] = ld_weights(wt + (size_t)u * GB + 16 * c);
+                if (FMT == kQ8F32) wsc[k] = ld_f32(static_cast<const float *>(p.ws) + s0 + u);
+                else hs[k] = ld_u16(static_cast<const uint16_t *>(p.ws) + s0 + u);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int u = base + k * kThreads;
+            if (u < units) {
+                int acc = 0;
+                if (FMT == kQ4F16) {
+                    const uint4 e = xplane[g], o = xplane[ng + g];
+                    const uint32_t w4[4] = {wv[k][0].x, wv[k][0].y, wv[k][0].z, wv[k][0].w};
+                    const uint32_t ev[4] = {e.x, e.y, e.z, e.w}, ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        // nibble v in [0, 15] -> v ^ 8 = int4 value + 8; corrected below by 8 * sum(x)
+                        const uint32_t lo = (w4[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
+                        const uint32_t hi = ((w4[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+                        acc = __dp4a((int)lo, (int)ev[j], acc);
+                        acc = __dp4a((int)hi, (int)ov[j], acc);
+                    }
+                    acc -= 8 * xsum_s[g];
+                } else {
+#pragma unroll
+                    for (int c = 0; c < WC; c++) {
+                        const uint4 a = xplane[c * ng + g];
+                        acc = __dp4a((int)wv[k][c].x, (int)a.x, acc);
+                        acc = __dp4a((int)wv[k][c].y, (int)a.y, acc);
+                        acc = __dp4a((int)wv[k][c].z, (int)a.z, acc);
+                        acc = __dp4a((int)wv[k][c].w, (int)a.w, acc);
+                    }
+                }
+                const float wscale = FMT == kQ8F32 ? wsc[k] : scale_from_f16(hs[k]);
+                prod[r * (ng + 1) + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), wscale), xs_s[g]);
+            }
+            g += dg;
+            r += dr;
+            if (g >= ng) { g -= ng; r++; }
+        }
+    }
+    __syncthreads();
+    allow_consumer();
+
+    // Row r's products in group order, exactly like the reference's `val += ...` loop.
+    if (tid < rows) {
+        const float *pr = prod + tid * (ng + 1);
+        float v = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < ng; j++) v = __fadd_rn(v, pr[j]);
+        p.out[row0 + tid] = v;
+    }
+}
+
+}  // namespace mvb

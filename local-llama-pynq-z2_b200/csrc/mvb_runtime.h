@@ -1,0 +1,20 @@
+// Shared host-side helpers of libmatvec_b200.so: error reporting and the matvec launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+
+namespace mvb {
+
+// Records the message for mvb_last_error() and prints it on stderr (the reference's drivers report there).
+void set_error(const char *fmt, ...) __attribute__((format(printf, 1, 2)));
+void clear_error();
+
+// Validates and launches one matvec. fmt: WeightFormat; gs: 32 or 64; xmode: XMode. pdl: launch with
+// programmatic dependent launch. Returns 0, or -1 after set_error(). `who` prefixes messages.
+int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *ws, const void *xq, const void *xs,
+                  const float *x, float *out, int n, int d, int xmode, cudaStream_t stream, bool pdl = false);
+
+int rows_per_tile(int n, int d);
+
+}  // namespace mvb
