@@ -41,6 +41,69 @@ int mvb_qmatvec(const void *wq, const void *ws, const float *x, float *out, int 
 /* Rows per CTA tile that the launchers pick for a d x n matrix (exposed for the benchmark's accounting). */
 int mvb_rows_per_tile(int n, int d);
 
+/* ---- Device-resident Qwen2 decode (the reference's token loop, qwen/qwen.c:490-712, on the device) ----
+ * The whole forward step (embedding, per-layer rmsnorm/quantize/matvecs/attention/SwiGLU, head, greedy argmax)
+ * runs on the current CUDA device as one captured CUDA graph, every matvec being this library's kernel. Token
+ * and position live in device memory, so a generation is one graph launch per position with no host work.
+ * All calls below are synchronous except mvb_qwen_rewind and mvb_qwen_launch, and wait at most
+ * MATVEC_TIMEOUT_S (default 5 s) plus 10 ms per position. */
+
+/* Uploads a .qwb image (the whole file's bytes, layout of tools/gguf2qwb.py:5-15) to the current device and
+ * captures the decode step; ctx is the KV-cache length (clipped to the header's max_seq_len like qwen.c:325,
+ * at most 8192). Returns a handle, or NULL with the reason in mvb_last_error(). */
+void *mvb_qwen_load(const void *qwb_image, size_t bytes, int ctx);
+
+/* out[0..8] = dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, head_k, ctx, kernels per step. */
+int mvb_qwen_config(void *model, int *out);
+
+/* The model's CUDA stream (every launch of the model is on it). */
+void *mvb_qwen_stream(void *model);
+
+/* One forward at `pos` with input `token` (qwen.c forward(), qwen.c:490-573); if logits is not NULL it receives
+ * the head_k head logits. Returns the greedy head row (argmax, first of ties), or -1. */
+int mvb_qwen_forward(void *model, int token, int pos, float *logits);
+
+/* Feeds prompt[0 .. n-2] at positions 0 .. n-2 and leaves prompt[n-1] as the input of position n-1, like
+ * qwen.c generate() before its first sampled token. 0, or -1. */
+int mvb_qwen_prefill(void *model, const int *prompt, int n);
+
+/* Greedy decode of `steps` tokens from the current state; their token ids go to ids (host). Returns steps or -1. */
+int mvb_qwen_decode(void *model, int steps, int *ids);
+
+/* qwen.c generate() at -t 0 (qwen.c:669-712): prefill, then greedy ids into ids (host) until `steps`, a stop
+ * token (<|im_end|>, <|endoftext|>, not copied) or a full context. Returns the number of ids, or -1. */
+int mvb_qwen_generate(void *model, const int *prompt, int n_prompt, int steps, int *ids);
+
+/* Sets the state to input `token` at position `pos` (positions below keep their KV cache), with n_prompt the
+ * prompt length for the prompt/greedy switch (negative: no sampling). Asynchronous on the model's stream (the
+ * state is copied from a pinned ring of 256 slots). Lets a benchmark repeat a decode from a filled cache. */
+int mvb_qwen_rewind(void *model, int token, int pos, int n_prompt);
+
+/* Runs one step with a CUDA event before every kernel and after the last (and no overlap between kernels),
+ * writing each kernel's duration in ms to ms[0 .. count-1] (cap >= kernels per step). Returns the count or -1. */
+int mvb_qwen_profile(void *model, float *ms, int cap);
+
+/* Kernel k of the step: its kind ("embed", "qkv", "attention", "o_proj", "gate_up", "down", "final_norm",
+ * "head", "next_token") into kind[kind_len], its layer (-1 outside the layers), and the bytes it must move at
+ * position pos (weights, scales, activations, KV-cache rows). 0, or -1. */
+int mvb_qwen_kernel_info(void *model, int k, int pos, char *kind, int kind_len, int *layer, double *bytes);
+
+/* One forward at (token, pos) that also copies the residual stream x into trace (host,
+ * (2 * n_layers + 1) * dim floats): after the embedding, then after each layer's attention and FFN blocks. */
+int mvb_qwen_trace(void *model, int token, int pos, float *trace);
+
+/* Enqueues `count` decode steps on the model's stream and returns without waiting. */
+int mvb_qwen_launch(void *model, int count);
+
+/* Frees the model's device memory, graph and stream. */
+void mvb_qwen_free(void *model);
+
+/* The decode's expf on n device inputs x -> y (device pointers, asynchronous on `stream`): bit-identical to the
+ * host C library's expf (the one qwen.c calls) on every float. The first call per process builds the table of
+ * the library's non-correctly-rounded results (all host threads, a few seconds; cached under $MVB_CACHE_DIR or
+ * /tmp). entries/thresh (may be NULL) receive the table size and probe threshold. 0, or -1. */
+int mvb_expf_eval(const float *x, float *y, int n, int *entries, float *thresh, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,6 +59,35 @@ def lib():
             f.argtypes = [vp] * 4 + [i] * 3 + [vp]
         L.mvb_rows_per_tile.restype = i
         L.mvb_rows_per_tile.argtypes = [i, i]
+        ip = C.POINTER(C.c_int)
+        L.mvb_qwen_load.restype = vp
+        L.mvb_qwen_load.argtypes = [vp, C.c_size_t, i]
+        L.mvb_qwen_config.restype = i
+        L.mvb_qwen_config.argtypes = [vp, ip]
+        L.mvb_qwen_stream.restype = vp
+        L.mvb_qwen_stream.argtypes = [vp]
+        L.mvb_qwen_forward.restype = i
+        L.mvb_qwen_forward.argtypes = [vp, i, i, vp]
+        L.mvb_qwen_prefill.restype = i
+        L.mvb_qwen_prefill.argtypes = [vp, ip, i]
+        L.mvb_qwen_decode.restype = i
+        L.mvb_qwen_decode.argtypes = [vp, i, ip]
+        L.mvb_qwen_generate.restype = i
+        L.mvb_qwen_generate.argtypes = [vp, ip, i, i, ip]
+        L.mvb_qwen_rewind.restype = i
+        L.mvb_qwen_rewind.argtypes = [vp, i, i, i]
+        L.mvb_qwen_launch.restype = i
+        L.mvb_qwen_launch.argtypes = [vp, i]
+        L.mvb_qwen_free.restype = None
+        L.mvb_qwen_free.argtypes = [vp]
+        L.mvb_expf_eval.restype = i
+        L.mvb_expf_eval.argtypes = [vp, vp, i, ip, C.POINTER(C.c_float), vp]
+        L.mvb_qwen_trace.restype = i
+        L.mvb_qwen_trace.argtypes = [vp, i, i, C.POINTER(C.c_float)]
+        L.mvb_qwen_profile.restype = i
+        L.mvb_qwen_profile.argtypes = [vp, C.POINTER(C.c_float), i]
+        L.mvb_qwen_kernel_info.restype = i
+        L.mvb_qwen_kernel_info.argtypes = [vp, i, i, C.c_char_p, i, ip, C.POINTER(C.c_double)]
         _bind_extra(L)
         _lib = L
     return _lib
@@ -169,3 +198,115 @@ def qmatvec(wq, ws, x, out, n, d, gs, stream=None):
 
 def rows_per_tile(n, d):
     return lib().mvb_rows_per_tile(n, d)
+
+
+def expf_device(x, y, stream=None):
+    """y = the decode's expf of x (float32 CUDA tensors); returns (table entries, probe threshold)."""
+    e, t = C.c_int(), C.c_float()
+    check(lib().mvb_expf_eval(_ptr(x), _ptr(y), x.numel(), C.byref(e), C.byref(t), _stream(stream)), "mvb_expf_eval")
+    return e.value, t.value
+
+
+# ---- device-resident Qwen2 decode (include/matvec_b200.h, mvb_qwen_*) ----
+
+class QwenDecoder:
+    """A .qwb model resident on the current CUDA device, decoding through the captured step graph."""
+
+    def __init__(self, path_or_bytes, ctx=1024):
+        import numpy as np
+        if isinstance(path_or_bytes, (bytes, bytearray, memoryview)):
+            img = np.frombuffer(path_or_bytes, np.uint8)
+        else:
+            img = np.fromfile(path_or_bytes, np.uint8)
+        self._img = img
+        h = lib().mvb_qwen_load(img.ctypes.data, img.nbytes, ctx)
+        if not h:
+            raise MatvecError("mvb_qwen_load failed: " + last_error())
+        self.h = h
+        cfg = (C.c_int * 9)()
+        lib().mvb_qwen_config(h, cfg)
+        keys = ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size", "head_k", "ctx",
+                "kernels_per_step")
+        self.cfg = dict(zip(keys, list(cfg)))
+
+    @staticmethod
+    def _ids(a):
+        import numpy as np
+        return np.ascontiguousarray(a, dtype=np.int32)
+
+    def forward(self, token, pos, want_logits=True):
+        """(greedy head row, logits or None) of one forward at `pos`."""
+        import numpy as np
+        lg = np.empty(self.cfg["head_k"], np.float32) if want_logits else None
+        row = lib().mvb_qwen_forward(self.h, int(token), int(pos), lg.ctypes.data if lg is not None else None)
+        if row < 0:
+            raise MatvecError("mvb_qwen_forward failed: " + last_error())
+        return row, lg
+
+    def prefill(self, prompt):
+        p = self._ids(prompt)
+        check(lib().mvb_qwen_prefill(self.h, p.ctypes.data_as(C.POINTER(C.c_int)), p.size), "mvb_qwen_prefill")
+
+    def decode(self, steps):
+        import numpy as np
+        out = np.empty(steps, np.int32)
+        if lib().mvb_qwen_decode(self.h, steps, out.ctypes.data_as(C.POINTER(C.c_int))) != steps:
+            raise MatvecError("mvb_qwen_decode failed: " + last_error())
+        return out
+
+    def generate(self, prompt, steps):
+        import numpy as np
+        p = self._ids(prompt)
+        out = np.empty(steps, np.int32)
+        n = lib().mvb_qwen_generate(self.h, p.ctypes.data_as(C.POINTER(C.c_int)), p.size, steps,
+                                    out.ctypes.data_as(C.POINTER(C.c_int)))
+        if n < 0:
+            raise MatvecError("mvb_qwen_generate failed: " + last_error())
+        return out[:n]
+
+    def rewind(self, token, pos, n_prompt):
+        check(lib().mvb_qwen_rewind(self.h, token, pos, n_prompt), "mvb_qwen_rewind")
+
+    def launch(self, count):
+        check(lib().mvb_qwen_launch(self.h, count), "mvb_qwen_launch")
+
+    def profile(self):
+        """Durations (ms) of every kernel of one instrumented step from the current state."""
+        import numpy as np
+        ms = np.zeros(self.cfg["kernels_per_step"], np.float32)
+        n = lib().mvb_qwen_profile(self.h, ms.ctypes.data_as(C.POINTER(C.c_float)), ms.size)
+        if n < 0:
+            raise MatvecError("mvb_qwen_profile failed: " + last_error())
+        return ms[:n]
+
+    def trace(self, token, pos):
+        """Residual stream after the embedding and after every attention / FFN block: [2 * n_layers + 1, dim]."""
+        import numpy as np
+        out = np.empty((2 * self.cfg["n_layers"] + 1, self.cfg["dim"]), np.float32)
+        check(lib().mvb_qwen_trace(self.h, int(token), int(pos), out.ctypes.data_as(C.POINTER(C.c_float))),
+              "mvb_qwen_trace")
+        return out
+
+    def kernel_info(self, pos):
+        """[(kind, layer, algorithmic bytes at position pos)] for every kernel of the step."""
+        out = []
+        for k in range(self.cfg["kernels_per_step"]):
+            kind, layer, b = C.create_string_buffer(32), C.c_int(), C.c_double()
+            check(lib().mvb_qwen_kernel_info(self.h, k, pos, kind, 32, C.byref(layer), C.byref(b)), "kernel_info")
+            out.append((kind.value.decode(), layer.value, b.value))
+        return out
+
+    @property
+    def stream_handle(self):
+        return lib().mvb_qwen_stream(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().mvb_qwen_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -29,8 +29,10 @@ import numpy as np
 
 QWEN05B = dict(dim=896, hidden_dim=4864, n_layers=24, n_heads=14, n_kv_heads=2, vocab_size=151936, head_k=65536,
                max_seq_len=32768, group_size=32, emb_bits=8, rope_theta=1e6, rms_eps=1e-6)
-# a small model with the same structure, for tests that must finish in seconds on the CPU oracle
-QWEN_TINY = dict(dim=128, hidden_dim=256, n_layers=2, n_heads=2, n_kv_heads=1, vocab_size=1000, head_k=512,
+# a small model with the same structure, for tests that must finish in seconds on the CPU oracle. qwen.c's
+# matvec output buffer holds max(dim, hidden_dim) floats (qwen.c:295-300) and every head block writes
+# min(head_k, 2048) of them, so head_k must not exceed hidden_dim here.
+QWEN_TINY = dict(dim=128, hidden_dim=256, n_layers=2, n_heads=2, n_kv_heads=1, vocab_size=1000, head_k=256,
                  max_seq_len=256, group_size=32, emb_bits=8, rope_theta=1e6, rms_eps=1e-6)
 
 STORIES15M = dict(dim=288, hidden_dim=768, n_layers=6, n_heads=6, n_kv_heads=6, vocab_size=32000, seq_len=256)

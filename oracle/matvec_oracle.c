@@ -135,3 +135,8 @@ void orc_matvec_f32(float *out, const int8_t *wq, const float *ws, const int8_t 
         out[i] = val;
     }
 }
+
+/* The host C library's expf over an array: the function qwen.c's softmax and SiLU call (qwen.c:350, :560). */
+void orc_expf_array(const float *x, float *y, long n) {
+    for (long i = 0; i < n; i++) y[i] = expf(x[i]);
+}

@@ -40,7 +40,15 @@ class Restatement:
         lib.orc_group_sums.argtypes = [_i32p, _u8p, _i8p, C.c_int, C.c_int, C.c_int, C.c_int]
         lib.orc_matvec_f16.argtypes = [_f32p, _u8p, _u16p, _i8p, _f32p, C.c_int, C.c_int, C.c_int]
         lib.orc_matvec_f32.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, C.c_int, C.c_int, C.c_int]
+        lib.orc_expf_array.argtypes = [_f32p, _f32p, C.c_long]
         self.lib = lib
+
+    def expf(self, x):
+        """The host C library's expf, elementwise."""
+        x = _c(x, np.float32)
+        y = np.empty_like(x)
+        self.lib.orc_expf_array(x, y, x.size)
+        return y
 
     def f16(self, h):
         return self.lib.orc_f16(int(h))
@@ -88,6 +96,7 @@ class RefQwen:
         lib.ref_qwen_quantize.argtypes = [_i8p, _f32p, _f32p, C.c_int]
         lib.ref_qwen_f16.restype = C.c_float
         lib.ref_qwen_f16.argtypes = [C.c_uint16]
+        lib.ref_qwen_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
         lib.ref_qwen_matmul_cpu.argtypes = [_f32p, _u8p, _u16p, _i8p, _f32p, C.c_int, C.c_int, C.c_int]
         lib.ref_qwen_open.argtypes = [C.c_char_p, C.c_int]
         lib.ref_qwen_config.argtypes = [C.POINTER(C.c_int)]
@@ -106,6 +115,12 @@ class RefQwen:
         q, s = np.empty(x.size, np.int8), np.empty(x.size // 32, np.float32)
         self.lib.ref_qwen_quantize(q, s, x, x.size)
         return q, s
+
+    def rmsnorm(self, x, w, eps):
+        x = _c(x, np.float32)
+        o = np.empty_like(x)
+        self.lib.ref_qwen_rmsnorm(o, x, _c(w, np.float32), x.size, eps)
+        return o
 
     def matmul_cpu(self, w, ws, xq, xs, n, d, bits):
         out = np.empty(d, np.float32)

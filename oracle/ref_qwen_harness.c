@@ -15,6 +15,8 @@ void ref_qwen_quantize(int8_t *q, float *s, const float *x, int n) { quantize(q,
 
 float ref_qwen_f16(uint16_t h) { return f16(h); }
 
+void ref_qwen_rmsnorm(float *o, const float *x, const float *w, int n, float eps) { rmsnorm(o, x, w, n, eps); }
+
 void ref_qwen_matmul_cpu(float *out, const uint8_t *w, const uint16_t *s, const int8_t *xq, const float *xs, int n,
                          int d, int bits) {
     Matrix m;
