@@ -98,6 +98,21 @@ int mvb_qwen_launch(void *model, int count);
 /* Frees the model's device memory, graph and stream. */
 void mvb_qwen_free(void *model);
 
+/* No counterpart in the reference. The decode's head path as one call that allocates nothing: rmsnorm of x with
+ * norm_w and eps (qwen.c:337-344), quantize (qwen.c:355-364), then fpga_matvec4's computation of w/ws (d rows,
+ * n columns, wbits 4 or 8) into out. All pointers are device pointers; the call is asynchronous on `stream`.
+ * For callers that cannot allocate device memory while they run: hosts that size every device buffer once at
+ * start-up (the reference's own qwen.c and runq.c carve all of theirs from one pre-sized pool), code on a
+ * latency-critical path where cudaMalloc's implicit device-wide synchronization would stall other work, and code
+ * inside a framework that owns the device allocator. Its scratch (the quantized activations) is a fixed device
+ * array of 2,304 bytes that every GPU using the library holds until the process exits, so n is at most 2048
+ * (larger n returns -1 with a message). The first call on each device looks up that array's address; make that
+ * first call before any stream capture. Every call overwrites the whole scratch it reads, so nothing has to be
+ * cleared between calls, but all calls on a device share the one array: calls that can run at the same time on
+ * one GPU (for example on two streams) race. Returns 0, or -1 with the reason in mvb_last_error(). */
+int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, const void *w, const void *ws, float *out,
+                            int n, int d, int wbits, void *stream);
+
 /* The decode's expf on n device inputs x -> y (device pointers, asynchronous on `stream`): bit-identical to the
  * host C library's expf (the one qwen.c calls) on every float. The first call per process builds the table of
  * the library's non-correctly-rounded results (all host threads, a few seconds; cached under $MVB_CACHE_DIR or

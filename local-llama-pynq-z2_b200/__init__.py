@@ -80,6 +80,8 @@ def lib():
         L.mvb_qwen_launch.argtypes = [vp, i]
         L.mvb_qwen_free.restype = None
         L.mvb_qwen_free.argtypes = [vp]
+        L.mvb_norm_matvec4_static.restype = i
+        L.mvb_norm_matvec4_static.argtypes = [vp, vp, C.c_float, vp, vp, vp, i, i, i, vp]
         L.mvb_expf_eval.restype = i
         L.mvb_expf_eval.argtypes = [vp, vp, i, ip, C.POINTER(C.c_float), vp]
         L.mvb_qwen_trace.restype = i
@@ -198,6 +200,13 @@ def qmatvec(wq, ws, x, out, n, d, gs, stream=None):
 
 def rows_per_tile(n, d):
     return lib().mvb_rows_per_tile(n, d)
+
+
+def norm_matvec4_static(x, norm_w, eps, w, ws, out, n, d, wbits, stream=None):
+    """rmsnorm + quantize + matvec4 on CUDA tensors with no device allocation (scratch in a fixed device array);
+    returns the C return code (0, or -1 with last_error())."""
+    return lib().mvb_norm_matvec4_static(_ptr(x), _ptr(norm_w), C.c_float(eps), _ptr(w), _ptr(ws), _ptr(out), n, d,
+                                         wbits, _stream(stream))
 
 
 def expf_device(x, y, stream=None):

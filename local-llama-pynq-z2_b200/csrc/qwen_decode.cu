@@ -27,6 +27,8 @@
 #include <string.h>
 #include <time.h>
 
+#include <map>
+#include <mutex>
 #include <vector>
 
 #include "../../include/matvec_b200.h"
@@ -1053,4 +1055,74 @@ extern "C" int mvb_qwen_generate(void *model, const int *prompt, int n_prompt, i
     for (int i = 0; i < n; i++)
         if (ids[i] == kImEnd || ids[i] == kEndOfText) return i;
     return n;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The decode's head path without any device allocation: final rmsnorm + quantize (norm_quant_kernel) into a
+// scratch that lives in a file-scope device array, then the head matvec reading it. For callers that cannot
+// allocate device memory (see mvb_norm_matvec4_static in include/matvec_b200.h).
+namespace mvb {
+namespace qwen {
+
+constexpr int kStaticNormMatvecMaxN = kMaxDim;  // 2048 columns
+// n int8 quantized activations at offset 0, their n/32 fp32 scales at offset kStaticNormMatvecMaxN
+static __device__ __align__(256) uint8_t g_norm_matvec_scratch[kStaticNormMatvecMaxN + kStaticNormMatvecMaxN / 32 * 4];
+
+static std::mutex g_scratch_mu;
+static std::map<int, uint8_t *> g_scratch_addr;  // device ordinal -> device address of the array
+
+// The array's device address on the current device, looked up once per device. Host code only has a stand-in
+// for the array's name; handing that to a kernel would read the wrong memory.
+static uint8_t *scratch_address(int dev) {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    auto it = g_scratch_addr.find(dev);
+    if (it != g_scratch_addr.end()) return it->second;
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_norm_matvec_scratch);
+    if (e != cudaSuccess || !p) {
+        set_error("mvb_norm_matvec4_static: cannot get the scratch address on device %d: %s", dev,
+                  cudaGetErrorString(e));
+        return nullptr;
+    }
+    g_scratch_addr[dev] = static_cast<uint8_t *>(p);
+    return static_cast<uint8_t *>(p);
+}
+
+}  // namespace qwen
+}  // namespace mvb
+
+extern "C" int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, const void *w, const void *ws,
+                                       float *out, int n, int d, int wbits, void *stream) {
+    using namespace mvb::qwen;
+    if (!x || !norm_w) {
+        set_error("mvb_norm_matvec4_static: null pointer argument");
+        return -1;
+    }
+    if (wbits != 4 && wbits != 8) {
+        set_error("mvb_norm_matvec4_static: unsupported wbits=%d (need 4 or 8)", wbits);
+        return -1;
+    }
+    if (n <= 0 || n % 32 || n > kStaticNormMatvecMaxN || d <= 0) {
+        set_error("mvb_norm_matvec4_static: unsupported n=%d d=%d: this entry point keeps its scratch in a fixed "
+                  "device array and takes at most n = %d columns (n %% 32 == 0, d >= 1)", n, d, kStaticNormMatvecMaxN);
+        return -1;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error("mvb_norm_matvec4_static: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    uint8_t *scratch = scratch_address(dev);
+    if (!scratch) return -1;
+    int8_t *xq = reinterpret_cast<int8_t *>(scratch);
+    float *xs = reinterpret_cast<float *>(scratch + kStaticNormMatvecMaxN);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    norm_quant_kernel<<<1, kThreads, 0, s>>>(x, norm_w, eps, n, xq, xs);
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+        set_error("mvb_norm_matvec4_static: launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return launch_matvec("mvb_norm_matvec4_static", wbits == 4 ? kQ4F16 : kQ8F16, 32, w, ws, xq, xs, nullptr, out, n,
+                         d, kXQuantized, s);
 }
