@@ -32,6 +32,7 @@
 #include <vector>
 
 #include "../../include/matvec_b200.h"
+#include "decode_kernels.cuh"
 #include "expf_ref.h"
 #include "matvec_kernels.cuh"
 #include "mvb_runtime.h"
@@ -39,35 +40,8 @@
 namespace mvb {
 namespace qwen {
 
-constexpr int kMaxDim = 2048;     // largest dim the fused prologues stage in shared memory
-constexpr int kMaxHead = 128;     // largest head size of the attention kernel
+constexpr int kMaxDim = 2048;     // largest dim the norm kernels stage in shared memory
 constexpr int kMaxCtx = 8192;     // largest context (attention scores live in shared memory)
-constexpr int kImEnd = 151645, kEndOfText = 151643;  // qwen.c:31-32
-
-struct State {
-    int token;       // token of the current position
-    int pos;         // current position
-    int n_prompt;    // prompt length; < 0: the host supplies every token (no prompt feeding, no sampling)
-    int n_gen;       // tokens generated so far
-    unsigned long long key;  // argmax of the head: (orderable logit << 32) | ~row
-    int last_row;    // head row of the last argmax
-    int pad;
-};
-
-
-// ---------------------------------------------------------------------------------------------------------------
-// embedding row (qwen.c:498-501): x[i] = er[i] * f16(es[i / 32]), exact in fp32
-__global__ void embed_kernel(const int8_t *emb_q, const uint16_t *emb_s, float *x, int dim, State *st) {
-    wait_for_producer();
-    const int tok = st->token;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i == 0) st->key = 0ull;
-    if (i < dim) {
-        const size_t r = (size_t)tok * dim;
-        x[i] = __fmul_rn(__int2float_rn(emb_q[r + i]), scale_from_f16(emb_s[r / 32 + i / 32]));
-    }
-    allow_consumer();
-}
 
 // ---------------------------------------------------------------------------------------------------------------
 // rmsnorm of qwen.c:337-344 into shared memory: ss = sum x^2 in order, ss = 1/sqrtf(ss/n + eps), o = w * (ss * x).
@@ -117,354 +91,6 @@ __global__ void __launch_bounds__(kThreads) norm_quant_kernel(const float *x, co
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// The fused decode matvec: prologue (rmsnorm and/or quantize into shared-memory planes), the group-product stream
-// of matvec_kernel over "virtual rows" (rows of up to three matrices), the in-order fold, then an epilogue.
-enum Epilogue : int {
-    kEpiStore = 0,     // out[row] = v
-    kEpiResidual = 1,  // out[row] += v                                    (qwen.c:551, :565)
-    kEpiSwiGLU = 2,    // tile = rows of w1 then the same rows of w3; out[row] = silu(g) * u   (qwen.c:558-562)
-    kEpiHead = 3,      // out[row] = v, plus the argmax key                 (qwen.c:571, 591-598)
-};
-
-struct FusedParams {
-    const uint8_t *w[3];
-    const uint16_t *ws[3];
-    int rows[3];        // rows of each matrix; the output row space is their concatenation (or the pair)
-    int n, rt, d;       // columns, output rows per tile, output rows in total
-    const float *x;        // fp32 activations to quantize (null: xq/xs given)
-    const float *norm_w;   // rmsnorm weight (null: no rmsnorm)
-    float eps;
-    const int8_t *xq;
-    const float *xs;
-    float *out;
-    State *st;
-    ExpTable et;           // the host library's expf (SiLU)
-};
-
-template <int BITS, int EPI>
-__global__ void __launch_bounds__(kThreads) fused_matvec_kernel(const FusedParams p) {
-    constexpr int GB = BITS == 4 ? 16 : 32;
-    constexpr int WC = GB / 16;
-    constexpr int K = BITS == 4 ? 4 : 2;
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int n = p.n, ng = n / 32, tid = threadIdx.x;
-    const int row0 = blockIdx.x * p.rt;
-    const int rows = min(p.rt, p.d - row0);
-    const int vrows = EPI == kEpiSwiGLU ? 2 * rows : rows;
-
-    // shared memory: planes | xs | xsum | prod[vrows][ng+1] | row pointers | staging floats for the prologue
-    uint4 *xplane = reinterpret_cast<uint4 *>(smem);
-    float *xs_s = reinterpret_cast<float *>(xplane + 2 * ng);
-    int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
-    float *prod = reinterpret_cast<float *>(xsum_s + ng);
-    const int vmax = EPI == kEpiSwiGLU ? 2 * p.rt : p.rt;
-    const uint8_t **wrow = reinterpret_cast<const uint8_t **>(
-        (reinterpret_cast<uintptr_t>(prod + (size_t)vmax * (ng + 1)) + 15) & ~(uintptr_t)15);
-    const uint16_t **srow = reinterpret_cast<const uint16_t **>(wrow + vmax);
-    float *stage = reinterpret_cast<float *>(srow + vmax);  // 2 * n floats when the prologue normalizes
-
-    // row pointers of this tile (weights are constant: set them up before waiting on the producer)
-    for (int vr = tid; vr < vrows; vr += kThreads) {
-        int m, r;
-        if (EPI == kEpiSwiGLU) {
-            m = vr < rows ? 0 : 1;
-            r = row0 + (vr < rows ? vr : vr - rows);
-        } else {
-            r = row0 + vr;
-            m = 0;
-            if (r >= p.rows[0]) { r -= p.rows[0]; m = 1; }
-            if (m == 1 && r >= p.rows[1]) { r -= p.rows[1]; m = 2; }
-        }
-        const uint8_t *wb = m == 0 ? p.w[0] : (m == 1 ? p.w[1] : p.w[2]);
-        const uint16_t *sb = m == 0 ? p.ws[0] : (m == 1 ? p.ws[1] : p.ws[2]);
-        wrow[vr] = wb + (size_t)r * ng * GB;
-        srow[vr] = sb + (size_t)r * ng;
-    }
-    wait_for_producer();
-
-    // prologue: activations into the planes
-    if (p.x) {
-        const float *src = p.x;
-        if (p.norm_w) {
-            rmsnorm_smem(stage, stage + n, p.x, p.norm_w, n, p.eps);
-            src = stage;
-        }
-        for (int g = tid; g < ng; g += kThreads) {
-            int8_t q[32];
-            xs_s[g] = quantize_group<32>(src, g, kXQuantizeQwen, q);
-            uint32_t wv[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++)
-                wv[j] = (uint32_t)(uint8_t)q[4 * j] | (uint32_t)(uint8_t)q[4 * j + 1] << 8 |
-                        (uint32_t)(uint8_t)q[4 * j + 2] << 16 | (uint32_t)(uint8_t)q[4 * j + 3] << 24;
-            if (BITS == 4) {
-                uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]);
-                uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]);
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    ev[j] = __byte_perm(wv[2 * j], wv[2 * j + 1], 0x6420);
-                    od[j] = __byte_perm(wv[2 * j], wv[2 * j + 1], 0x7531);
-                }
-            } else {
-                xplane[g] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                xplane[ng + g] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
-            }
-        }
-    } else {
-        for (int c = tid; c < n / 16; c += kThreads) {
-            const uint4 a = *reinterpret_cast<const uint4 *>(p.xq + 16 * c);
-            const int g = c >> 1, k = c & 1;
-            if (BITS == 4) {
-                uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
-                uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
-                ev[0] = __byte_perm(a.x, a.y, 0x6420);
-                ev[1] = __byte_perm(a.z, a.w, 0x6420);
-                od[0] = __byte_perm(a.x, a.y, 0x7531);
-                od[1] = __byte_perm(a.z, a.w, 0x7531);
-            } else {
-                xplane[k * ng + g] = a;
-            }
-        }
-        for (int g = tid; g < ng; g += kThreads) xs_s[g] = p.xs[g];
-    }
-    __syncthreads();
-    if (BITS == 4) {
-        for (int g = tid; g < ng; g += kThreads) {
-            const uint4 e = xplane[g], o = xplane[ng + g];
-            int s = __dp4a((int)e.x, 0x01010101, 0);
-            s = __dp4a((int)e.y, 0x01010101, s);
-            s = __dp4a((int)e.z, 0x01010101, s);
-            s = __dp4a((int)e.w, 0x01010101, s);
-            s = __dp4a((int)o.x, 0x01010101, s);
-            s = __dp4a((int)o.y, 0x01010101, s);
-            s = __dp4a((int)o.z, 0x01010101, s);
-            s = __dp4a((int)o.w, 0x01010101, s);
-            xsum_s[g] = s;
-        }
-        __syncthreads();
-    }
-
-    // group products of the tile's virtual rows
-    const int units = vrows * ng;
-    int r = tid / ng, g = tid % ng;
-    const int dr = kThreads / ng, dg = kThreads % ng;
-    for (int base = tid; base < units; base += K * kThreads) {
-        uint4 wv[K][WC];
-        uint32_t hs[K];
-        int rr = r, gg = g;
-#pragma unroll
-        for (int k = 0; k < K; k++) {
-            if (base + k * kThreads < units) {
-                const uint8_t *src = wrow[rr] + (size_t)gg * GB;
-#pragma unroll
-                for (int c = 0; c < WC; c++) wv[k][c] = ld_weights(src + 16 * c);
-                hs[k] = ld_u16(srow[rr] + gg);
-            }
-            gg += dg;
-            rr += dr;
-            if (gg >= ng) { gg -= ng; rr++; }
-        }
-#pragma unroll
-        for (int k = 0; k < K; k++) {
-            if (base + k * kThreads < units) {
-                int acc = 0;
-                if (BITS == 4) {
-                    const uint4 e = xplane[g], o = xplane[ng + g];
-                    const uint32_t w4[4] = {wv[k][0].x, wv[k][0].y, wv[k][0].z, wv[k][0].w};
-                    const uint32_t ev[4] = {e.x, e.y, e.z, e.w}, ov[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const uint32_t lo = (w4[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
-                        const uint32_t hi = ((w4[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-                        acc = __dp4a((int)lo, (int)ev[j], acc);
-                        acc = __dp4a((int)hi, (int)ov[j], acc);
-                    }
-                    acc -= 8 * xsum_s[g];
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 2; c++) {
-                        const uint4 a = xplane[c * ng + g];
-                        acc = __dp4a((int)wv[k][c].x, (int)a.x, acc);
-                        acc = __dp4a((int)wv[k][c].y, (int)a.y, acc);
-                        acc = __dp4a((int)wv[k][c].z, (int)a.z, acc);
-                        acc = __dp4a((int)wv[k][c].w, (int)a.w, acc);
-                    }
-                }
-                prod[r * (ng + 1) + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), scale_from_f16(hs[k])), xs_s[g]);
-            }
-            g += dg;
-            r += dr;
-            if (g >= ng) { g -= ng; r++; }
-        }
-    }
-    __syncthreads();
-    allow_consumer();
-
-    // in-order fold of each virtual row, then the epilogue
-    float v = 0.0f;
-    if (tid < vrows) {
-        const float *pr = prod + tid * (ng + 1);
-#pragma unroll 8
-        for (int j = 0; j < ng; j++) v = __fadd_rn(v, pr[j]);
-    }
-    if (EPI == kEpiStore) {
-        if (tid < rows) p.out[row0 + tid] = v;
-    } else if (EPI == kEpiResidual) {
-        if (tid < rows) p.out[row0 + tid] = __fadd_rn(p.out[row0 + tid], v);
-    } else if (EPI == kEpiSwiGLU) {
-        __syncthreads();  // prod is reused for the fold values
-        if (tid < vrows) prod[tid] = v;
-        __syncthreads();
-        if (tid < rows) {
-            float gv = prod[tid];
-            const float u = prod[rows + tid];
-            gv = __fmul_rn(gv, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-gv, p.et))));
-            p.out[row0 + tid] = __fmul_rn(gv, u);
-        }
-    } else {  // kEpiHead
-        unsigned long long key = 0ull;
-        if (tid < rows) {
-            p.out[row0 + tid] = v;
-            const float c = v == 0.0f ? 0.0f : v;  // -0 ties with +0, as the reference's `>` sees them
-            const uint32_t b = __float_as_uint(c);
-            const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-            if (c == c) key = ((unsigned long long)ord << 32) | (uint32_t)(~(uint32_t)(row0 + tid));
-        }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
-            key = o > key ? o : key;
-        }
-        if ((tid & 31) == 0 && tid < ((rows + 31) & ~31) && key) atomicMax(&p.st->key, key);
-    }
-}
-
-inline size_t fused_smem_bytes(int n, int rt, int epi, bool normalize) {
-    const int ng = n / 32;
-    const int vmax = epi == kEpiSwiGLU ? 2 * rt : rt;
-    size_t b = (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)vmax * (ng + 1) * 4;
-    b = (b + 15) & ~(size_t)15;
-    b += (size_t)vmax * 16;
-    if (normalize) b += (size_t)2 * n * 4;
-    return b;
-}
-
-// ---------------------------------------------------------------------------------------------------------------
-// attention for one query head (qwen.c:521-546): biases, NeoX RoPE (pairs i, i + hs/2), the KV-cache write of
-// this position, scores q.k / sqrt(hs) in order over the head's elements, softmax in order, weighted values in
-// order of position.
-struct AttnParams {
-    const float *qkv;   // raw outputs of the qkv matvec: q (dim) | k (kv_dim) | v (kv_dim)
-    const float *bq, *bk, *bv;
-    const float *rope;  // per position: cos[hs/2] then sin[hs/2]
-    float *kcache, *vcache;  // this layer's (ctx, kv_dim)
-    float *xb;          // dim outputs
-    int dim, kv_dim, hs, kv_mul;
-    State *st;
-    ExpTable et;        // the host library's expf (softmax)
-};
-
-__global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p) {
-    __shared__ __align__(16) float q[kMaxHead], kc[kMaxHead], vc[kMaxHead];
-    __shared__ __align__(16) float att[kMaxCtx];
-    __shared__ float red[kThreads / 32];
-    __shared__ float s_max, s_sum;
-    const int h = blockIdx.x, kvh = h / p.kv_mul, hs = p.hs, half = hs / 2, tid = threadIdx.x;
-    wait_for_producer();
-    const int pos = p.st->pos;
-    const float *cs = p.rope + (size_t)pos * hs;
-    const float *qr = p.qkv + h * hs, *kr = p.qkv + p.dim + kvh * hs, *vr = p.qkv + p.dim + p.kv_dim + kvh * hs;
-    if (tid < half) {
-        const float c = cs[tid], s = cs[half + tid];
-        float a = __fadd_rn(qr[tid], p.bq[h * hs + tid]), b = __fadd_rn(qr[tid + half], p.bq[h * hs + tid + half]);
-        q[tid] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        q[tid + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-        a = __fadd_rn(kr[tid], p.bk[kvh * hs + tid]);
-        b = __fadd_rn(kr[tid + half], p.bk[kvh * hs + tid + half]);
-        kc[tid] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        kc[tid + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-    }
-    if (tid < hs) vc[tid] = __fadd_rn(vr[tid], p.bv[kvh * hs + tid]);
-    __syncthreads();
-    if (h % p.kv_mul == 0 && tid < hs) {  // one writer per kv head
-        p.kcache[(size_t)pos * p.kv_dim + kvh * hs + tid] = kc[tid];
-        p.vcache[(size_t)pos * p.kv_dim + kvh * hs + tid] = vc[tid];
-    }
-    // scores
-    const float scale = __fsqrt_rn((float)hs);
-    for (int t = tid; t <= pos; t += kThreads) {
-        const float *kt = t == pos ? kc : p.kcache + (size_t)t * p.kv_dim + kvh * hs;
-        float score = 0.0f;
-        for (int i = 0; i < hs; i += 4) {
-            const float4 k4 = *reinterpret_cast<const float4 *>(kt + i);
-            score = __fadd_rn(score, __fmul_rn(q[i], k4.x));
-            score = __fadd_rn(score, __fmul_rn(q[i + 1], k4.y));
-            score = __fadd_rn(score, __fmul_rn(q[i + 2], k4.z));
-            score = __fadd_rn(score, __fmul_rn(q[i + 3], k4.w));
-        }
-        att[t] = __fdiv_rn(score, scale);
-    }
-    __syncthreads();
-    // softmax (qwen.c:346-352): max, exp(x - max), in-order sum, divide
-    float m = -INFINITY;
-    for (int t = tid; t <= pos; t += kThreads) m = fmaxf(m, att[t]);
-#pragma unroll
-    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if ((tid & 31) == 0) red[tid >> 5] = m;
-    __syncthreads();
-    if (tid == 0) {
-        float mm = red[0];
-        for (int w = 1; w < kThreads / 32; w++) mm = fmaxf(mm, red[w]);
-        s_max = mm;
-    }
-    __syncthreads();
-    const float mx = s_max;
-    for (int t = tid; t <= pos; t += kThreads) att[t] = expf_ref(__fsub_rn(att[t], mx), p.et);
-    __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;
-        for (int t = 0; t <= pos; t++) sum = __fadd_rn(sum, att[t]);
-        s_sum = sum;
-    }
-    __syncthreads();
-    const float sum = s_sum;
-    for (int t = tid; t <= pos; t += kThreads) att[t] = __fdiv_rn(att[t], sum);
-    __syncthreads();
-    allow_consumer();
-    // weighted values, in order of position
-    if (tid < hs) {
-        float acc = 0.0f;
-        const float *vcol = p.vcache + kvh * hs + tid;
-        for (int t = 0; t < pos; t++) acc = __fadd_rn(acc, __fmul_rn(att[t], vcol[(size_t)t * p.kv_dim]));
-        acc = __fadd_rn(acc, __fmul_rn(att[pos], vc[tid]));
-        p.xb[h * hs + tid] = acc;
-    }
-}
-
-// next token (qwen.c:674-700): the prompt while it lasts, then the greedy head row's token id
-__global__ void next_token_kernel(State *st, const int *prompt, const int32_t *head_ids, int *ids, int cap) {
-    wait_for_producer();
-    if (threadIdx.x != 0) return;
-    const int pos = st->pos;
-    const unsigned long long key = st->key;
-    // no key: every logit was NaN; the reference's strict `>` then keeps row 0 (qwen.c:591-598)
-    const int row = key ? (int)(~(uint32_t)(key & 0xffffffffu)) : 0;
-    st->last_row = row;
-    if (st->n_prompt >= 0) {
-        int next;
-        if (pos + 1 < st->n_prompt) {
-            next = prompt[pos + 1];
-        } else {
-            next = head_ids[row];
-            if (st->n_gen < cap) ids[st->n_gen] = next;
-            st->n_gen++;
-        }
-        st->token = next;
-    }
-    st->pos = pos + 1;
-}
-
-// ---------------------------------------------------------------------------------------------------------------
 struct Config {
     int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, head_k, max_seq_len, group_size, emb_bits;
     float rope_theta, rms_eps;
@@ -489,8 +115,11 @@ struct Model {
     std::vector<Mat> wq, wk, wv, wo, w1, w2, w3;
     Mat head, emb;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *hb = nullptr, *logits = nullptr, *kcache = nullptr,
-          *vcache = nullptr, *rope = nullptr, *xs = nullptr;
-    int8_t *xq = nullptr;
+          *vcache = nullptr, *rope = nullptr;
+    // the final normalized x, quantized once for the head by the last layer's down projection
+    int8_t *xq_n = nullptr;
+    float *xs_n = nullptr;
+    int *counters = nullptr;  // one last-CTA counter per kernel of the step
     int *prompt = nullptr, *ids = nullptr;
     State *st = nullptr;
     int kernels_per_step = 0;
@@ -531,17 +160,26 @@ static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
-template <int BITS, int EPI>
-static cudaError_t launch_fused(Model &m, FusedParams p, int *count) {
-    const bool norm = p.norm_w != nullptr;
-    const size_t smem = fused_smem_bytes(p.n, p.rt, EPI, norm);
+// Rows per tile for a decode matvec: `target`, or fewer so that the tile's groups fit UPT per thread.
+static int decode_rt(int target, int n, int upt, bool pair) {
+    const int per_row = (n / 32) * (pair ? 2 : 1);
+    const int lim = kThreads * upt / per_row;
+    return target < lim ? target : lim;
+}
+
+template <int BITS, int EPI, int PRO, int TAIL, int UPT>
+static cudaError_t launch_decode(Model &m, DecodeParams p, int *count) {
+    const size_t smem = decode_smem_bytes(p.n, p.rt, EPI, PRO, TAIL, p.d);
+    p.counter = m.counters + *count;
     (*count)++;
-    return launch(fused_matvec_kernel<BITS, EPI>, dim3((p.d + p.rt - 1) / p.rt), dim3(kThreads), smem, m.stream,
-                  m.pdl, p);
+    return launch(decode_matvec_kernel<BITS, EPI, PRO, TAIL, UPT>, dim3((p.d + p.rt - 1) / p.rt), dim3(kThreads),
+                  smem, m.stream, m.pdl, p);
 }
 
 // Enqueues one forward step on m.stream (captured into a graph by the caller). With `ev`, records ev[k] before
-// kernel k and ev[count] after the last one; `info` receives each kernel's kind and layer.
+// kernel k and ev[count] after the last one; `info` receives each kernel's kind and layer; with `trace`, the
+// residual stream x is copied out after the embedding (slot 0) and after each layer's attention (2l + 1) and FFN
+// (2l + 2).
 static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
                                 std::vector<Model::Info> *info = nullptr, float *trace = nullptr) {
     const Config &c = m.c;
@@ -552,82 +190,81 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
         if (info) info->push_back(Model::Info{kind, layer});
         return ev ? cudaEventRecordWithFlags(ev[*count], m.stream, cudaEventRecordExternal) : cudaSuccess;
     };
-    // with `trace`, x is copied out after each residual update: trace[0] after the embedding, then per layer
-    // after attention (2l + 1) and after the FFN (2l + 2)
     auto snap = [&](int slot) -> cudaError_t {
         return trace ? cudaMemcpyAsync(trace + (size_t)slot * c.dim, m.x, c.dim * 4, cudaMemcpyDeviceToDevice,
                                        m.stream)
                      : cudaSuccess;
     };
+    const int dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, L = c.n_layers;
     if ((e = mark("embed", -1)) != cudaSuccess) return e;
-    e = launch(embed_kernel, dim3((c.dim + 255) / 256), dim3(256), 0, m.stream, m.pdl, (const int8_t *)m.emb.w,
-               m.emb.s, m.x, c.dim, m.st);
+    e = launch(embed_kernel, dim3((dim + kThreads - 1) / kThreads), dim3(kThreads), 0, m.stream, m.pdl,
+               (const int8_t *)m.emb.w, m.emb.s, m.x, dim, m.st);
     (*count)++;
     if (e != cudaSuccess || (e = snap(0)) != cudaSuccess) return e;
-    const int dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim;
-    for (int l = 0; l < c.n_layers; l++) {
-        FusedParams p = {};
-        // qkv: rmsnorm + quantize + [wq; wk; wv]
+    for (int l = 0; l < L; l++) {
+        // qkv: rmsnorm + quantize of x in every CTA, then [wq; wk; wv] rows
+        DecodeParams p = {};
         p.w[0] = m.wq[l].w; p.ws[0] = m.wq[l].s; p.rows[0] = dim;
         p.w[1] = m.wk[l].w; p.ws[1] = m.wk[l].s; p.rows[1] = kv;
         p.w[2] = m.wv[l].w; p.ws[2] = m.wv[l].s; p.rows[2] = kv;
-        p.n = dim; p.d = dim + 2 * kv; p.rt = 8;
-        p.x = m.x; p.norm_w = m.attn_norm + (size_t)l * dim; p.eps = c.rms_eps;
-        p.out = m.qkv; p.st = m.st;
-        if ((e = mark("qkv", l)) != cudaSuccess || (e = launch_fused<4, kEpiStore>(m, p, count)) != cudaSuccess)
+        p.n = dim; p.d = dim + 2 * kv; p.rt = decode_rt(8, dim, 1, false);
+        p.src = m.x; p.norm_w = m.attn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.qkv; p.st = m.st;
+        if ((e = mark("qkv", l)) != cudaSuccess ||
+            (e = launch_decode<4, kEpiStore, kProNorm, kTailNone, 1>(m, p, count)) != cudaSuccess)
             return e;
         // attention
-        AttnParams a;
+        AttnParams a = {};
         a.qkv = m.qkv;
         a.bq = m.bq + (size_t)l * dim; a.bk = m.bk + (size_t)l * kv; a.bv = m.bv + (size_t)l * kv;
         a.rope = m.rope;
         a.kcache = m.kcache + (size_t)l * m.ctx * kv; a.vcache = m.vcache + (size_t)l * m.ctx * kv;
-        a.xb = m.xb; a.dim = dim; a.kv_dim = kv; a.hs = m.hs; a.kv_mul = c.n_heads / c.n_kv_heads; a.st = m.st;
+        a.xb = m.xb; a.dim = dim; a.kv_dim = kv; a.kv_mul = c.n_heads / c.n_kv_heads; a.ctx = m.ctx; a.st = m.st;
         a.et = m.et;
         if ((e = mark("attention", l)) != cudaSuccess) return e;
-        if ((e = launch(attention_kernel, dim3(c.n_heads), dim3(kThreads), 0, m.stream, m.pdl, a)) != cudaSuccess)
+        if ((e = launch(attention_kernel<64>, dim3(c.n_heads), dim3(kThreads), attention_smem_bytes<64>(m.ctx),
+                        m.stream, m.pdl, a)) != cudaSuccess)
             return e;
         (*count)++;
-        // o: quantize(xb) + wo, x += out
-        p = FusedParams{};
+        // o: quantize the attention output in every CTA, x += wo * it
+        p = DecodeParams{};
         p.w[0] = m.wo[l].w; p.ws[0] = m.wo[l].s; p.rows[0] = dim;
-        p.n = dim; p.d = dim; p.rt = 8; p.x = m.xb; p.out = m.x; p.st = m.st;
-        if ((e = mark("o_proj", l)) != cudaSuccess || (e = launch_fused<4, kEpiResidual>(m, p, count)) != cudaSuccess ||
+        p.n = dim; p.d = dim; p.rt = decode_rt(8, dim, 1, false);
+        p.src = m.xb; p.out = m.x; p.st = m.st;
+        if ((e = mark("o_proj", l)) != cudaSuccess ||
+            (e = launch_decode<4, kEpiResidual, kProQuant, kTailNone, 1>(m, p, count)) != cudaSuccess ||
             (e = snap(2 * l + 1)) != cudaSuccess)
             return e;
-        // gate/up: rmsnorm + quantize + (w1, w3) paired rows, SwiGLU -> hb
-        p = FusedParams{};
+        // gate/up: rmsnorm + quantize of x in every CTA, paired rows, SwiGLU -> hb
+        p = DecodeParams{};
         p.w[0] = m.w1[l].w; p.ws[0] = m.w1[l].s; p.rows[0] = hid;
         p.w[1] = m.w3[l].w; p.ws[1] = m.w3[l].s; p.rows[1] = hid;
-        p.n = dim; p.d = hid; p.rt = 16;
-        p.x = m.x; p.norm_w = m.ffn_norm + (size_t)l * dim; p.eps = c.rms_eps;
-        p.out = m.hb; p.st = m.st; p.et = m.et;
-        if ((e = mark("gate_up", l)) != cudaSuccess || (e = launch_fused<4, kEpiSwiGLU>(m, p, count)) != cudaSuccess)
+        p.n = dim; p.d = hid; p.rt = decode_rt(16, dim, 4, true);
+        p.src = m.x; p.norm_w = m.ffn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.hb; p.st = m.st;
+        p.et = m.et;
+        if ((e = mark("gate_up", l)) != cudaSuccess ||
+            (e = launch_decode<4, kEpiSwiGLU, kProNorm, kTailNone, 4>(m, p, count)) != cudaSuccess)
             return e;
-        // down: quantize(hb) + w2, x += out
-        p = FusedParams{};
+        // down: quantize hb in every CTA, x += w2 * it; after the last layer, the last CTA normalizes x for the head
+        p = DecodeParams{};
         p.w[0] = m.w2[l].w; p.ws[0] = m.w2[l].s; p.rows[0] = dim;
-        p.n = hid; p.d = dim; p.rt = 8; p.x = m.hb; p.out = m.x; p.st = m.st;
-        if ((e = mark("down", l)) != cudaSuccess || (e = launch_fused<4, kEpiResidual>(m, p, count)) != cudaSuccess ||
-            (e = snap(2 * l + 2)) != cudaSuccess)
-            return e;
+        p.n = hid; p.d = dim; p.rt = decode_rt(8, hid, 5, false);
+        p.src = m.hb; p.out = m.x; p.st = m.st;
+        p.tail_norm = m.out_norm; p.eps = c.rms_eps; p.tail_xq = m.xq_n; p.tail_xs = m.xs_n;
+        if ((e = mark("down", l)) != cudaSuccess) return e;
+        e = l + 1 < L ? launch_decode<4, kEpiResidual, kProQuant, kTailNone, 5>(m, p, count)
+                      : launch_decode<4, kEpiResidual, kProQuant, kTailNormQuant, 5>(m, p, count);
+        if (e != cudaSuccess || (e = snap(2 * l + 2)) != cudaSuccess) return e;
     }
-    // final norm + quantize, head, next token
-    if ((e = mark("final_norm", -1)) != cudaSuccess) return e;
-    if ((e = launch(norm_quant_kernel, dim3(1), dim3(kThreads), 0, m.stream, m.pdl, m.x, m.out_norm, c.rms_eps, dim,
-                    m.xq, m.xs)) != cudaSuccess)
-        return e;
-    (*count)++;
-    FusedParams p = {};
+    // head: logits + argmax; the last CTA picks the next token
+    DecodeParams p = {};
     p.w[0] = m.head.w; p.ws[0] = m.head.s; p.rows[0] = c.head_k;
-    p.n = dim; p.d = c.head_k; p.rt = 32; p.xq = m.xq; p.xs = m.xs; p.out = m.logits; p.st = m.st;
-    if ((e = mark("head", -1)) != cudaSuccess || (e = launch_fused<8, kEpiHead>(m, p, count)) != cudaSuccess)
+    p.n = dim; p.d = c.head_k; p.rt = decode_rt(32, dim, 4, false);
+    p.xq = m.xq_n; p.xs = m.xs_n; p.out = m.logits; p.st = m.st;
+    p.prompt = m.prompt; p.head_ids = m.head_ids; p.ids = m.ids; p.cap = m.ctx;
+    if ((e = mark("head", -1)) != cudaSuccess ||
+        (e = launch_decode<8, kEpiHead, kProQuantized, kTailNextToken, 4>(m, p, count)) != cudaSuccess)
         return e;
-    if ((e = mark("next_token", -1)) != cudaSuccess) return e;
-    e = launch(next_token_kernel, dim3(1), dim3(32), 0, m.stream, m.pdl, m.st, (const int *)m.prompt, m.head_ids,
-               m.ids, m.ctx);
-    (*count)++;
-    if (e == cudaSuccess && ev) e = cudaEventRecordWithFlags(ev[*count], m.stream, cudaEventRecordExternal);
+    if (ev) e = cudaEventRecordWithFlags(ev[*count], m.stream, cudaEventRecordExternal);
     return e;
 }
 
@@ -635,19 +272,21 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
 // (weights and scales, activations in and out, norm weights, KV-cache rows read and written).
 static double kernel_bytes(const Model &m, int k, int pos) {
     const Config &c = m.c;
-    const double dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, ng = dim / 32, ngh = hid / 32;
+    const double dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, ng = dim / 32;
     const char *kind = m.info[k].kind;
     auto q4 = [](double d, double n) { return d * n / 2 + d * (n / 32) * 2; };
     if (!strcmp(kind, "embed")) return dim + ng * 2 + dim * 4;
+    // matvecs: weights + scales, int8 input + scales, outputs (read + write for residual updates); tails: the
+    // vector they normalize or quantize, the norm weight, the int8 output
+    const bool last = m.info[k].layer == c.n_layers - 1;
     if (!strcmp(kind, "qkv")) return q4(dim + 2 * kv, dim) + dim * 4 * 2 + (dim + 2 * kv) * 4;
     if (!strcmp(kind, "attention"))
         return (dim + 2 * kv) * 4 * 2 + m.hs * 4 + 2.0 * pos * kv * 4 + 2 * kv * 4 + dim * 4;
     if (!strcmp(kind, "o_proj")) return q4(dim, dim) + dim * 4 + dim * 8;
     if (!strcmp(kind, "gate_up")) return 2 * q4(hid, dim) + dim * 4 * 2 + hid * 4;
-    if (!strcmp(kind, "down")) return q4(dim, hid) + hid * 4 + dim * 8;
-    if (!strcmp(kind, "final_norm")) return dim * 4 * 2 + dim + ng * 4;
-    if (!strcmp(kind, "head")) return (double)c.head_k * dim + (double)c.head_k * ng * 2 + dim + ng * 4 + c.head_k * 4.0;
-    (void)ngh;
+    if (!strcmp(kind, "down")) return q4(dim, hid) + hid * 4 + dim * 8 + (last ? dim * 4 * 2 + dim + ng * 4 : 0);
+    if (!strcmp(kind, "head"))
+        return (double)c.head_k * dim + (double)c.head_k * ng * 2 + dim + ng * 4 + c.head_k * 4.0;
     return 16;
 }
 
@@ -658,8 +297,8 @@ static void destroy(Model *m) {
     if (m->prof_graph) cudaGraphExecDestroy(m->prof_graph);
     for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     if (m->ring) cudaFreeHost(m->ring);
-    void *bufs[] = {m->image, m->x, m->xb, m->qkv, m->hb, m->logits, m->kcache, m->vcache, m->rope, m->xs, m->xq,
-                    m->prompt, m->ids, m->st};
+    void *bufs[] = {m->image, m->x, m->xb, m->qkv, m->hb, m->logits, m->kcache, m->vcache, m->rope, m->xq_n,
+                    m->xs_n, m->counters, m->prompt, m->ids, m->st};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -720,10 +359,11 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
     // qwen.c:223-228's checks, plus this implementation's own limits
     if (c.group_size != 32 || c.emb_bits != 8 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.dim % c.n_heads ||
         c.n_heads % c.n_kv_heads || (c.dim / c.n_heads) % 2 || c.dim % 128 || c.hidden_dim % 128 ||
-        (c.dim / c.n_heads * c.n_kv_heads) % 16 || c.dim > kMaxDim || c.hidden_dim > kMaxN || c.dim / c.n_heads > kMaxHead ||
-        (c.dim / c.n_heads) % 4 || c.head_k <= 0 || c.vocab_size <= 0 || c.n_layers <= 0) {
-        set_error("mvb_qwen_load: unsupported config (group %d, embedding %d-bit, dim %d, hidden %d, heads %d/%d)",
-                  c.group_size, c.emb_bits, c.dim, c.hidden_dim, c.n_heads, c.n_kv_heads);
+        (c.dim / c.n_heads * c.n_kv_heads) % 16 || c.dim > kMaxDim || c.hidden_dim > kMaxN || c.dim / c.n_heads != 64 ||
+        c.head_k <= 0 || c.vocab_size <= 0 || c.n_layers <= 0) {
+        set_error("mvb_qwen_load: unsupported config (group %d, embedding %d-bit, dim %d, hidden %d, heads %d/%d; "
+                  "this decode needs head size 64, dim <= %d, hidden <= %d)", c.group_size, c.emb_bits, c.dim,
+                  c.hidden_dim, c.n_heads, c.n_kv_heads, kMaxDim, kMaxN);
         delete m;
         return nullptr;
     }
@@ -803,14 +443,18 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
         (e = cudaMalloc(&m->logits, (size_t)c.head_k * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->kcache, kvbytes)) != cudaSuccess || (e = cudaMalloc(&m->vcache, kvbytes)) != cudaSuccess ||
         (e = cudaMalloc(&m->rope, rope.size() * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->xq, dim)) != cudaSuccess || (e = cudaMalloc(&m->xs, dim / 32 * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->xq_n, dim)) != cudaSuccess || (e = cudaMalloc(&m->xs_n, dim / 32 * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->counters, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->prompt, (size_t)m->ctx * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->ids, (size_t)m->ctx * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->st, sizeof(State))) != cudaSuccess)
         return fail("buffers");
     if ((e = cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
         (e = cudaMemset(m->kcache, 0, kvbytes)) != cudaSuccess || (e = cudaMemset(m->vcache, 0, kvbytes)) != cudaSuccess ||
-        (e = cudaMemset(m->st, 0, sizeof(State))) != cudaSuccess)
+        (e = cudaMemset(m->st, 0, sizeof(State))) != cudaSuccess ||
+        (e = cudaMemset(m->counters, 0, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attention_smem_bytes<64>(m->ctx))) != cudaSuccess)
         return fail("init");
     if ((e = cudaHostAlloc(&m->ring, sizeof(State) * Model::kRing, cudaHostAllocDefault)) != cudaSuccess)
         return fail("pinned state");
