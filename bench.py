@@ -270,6 +270,147 @@ def our_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+# ---- isolated-kernel modes (not the driver's default line) ----
+
+def _alg_bytes(n, d, bits, scale_bytes=2, gs=32):
+    """Algorithmic bytes of one matvec call: weights, scales, int8 activations + scales, fp32 outputs."""
+    return d * n * bits // 8 + d * (n // gs) * scale_bytes + n + (n // gs) * 4 + 4 * d
+
+
+def _rand_matrix(torch, n, d, bits, copies, gen):
+    w = [torch.randint(0, 256, (d * n * bits // 8,), dtype=torch.uint8, device="cuda", generator=gen)
+         for _ in range(copies)]
+    # fp16 scales in [1e-3, 2e-2] as bit patterns
+    s = [(torch.rand(d * (n // 32), device="cuda", generator=gen) * 0.019 + 0.001).half().view(torch.int16)
+         for _ in range(copies)]
+    return w, s
+
+
+def _time_graph(torch, fn, reps):
+    """Per-call device time (s) of fn() captured reps times in one CUDA graph (host launch cost excluded)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            fn(i)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(5):
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1000.0 / reps)
+    del g
+    return statistics.median(times)
+
+
+def sweep_mode(args):
+    """Config 4: the isolated matvec at the Qwen2.5-0.5B layer shapes and the heads, plus the large sharded
+    matrix on one GPU; inputs rotate through copies larger than 2x L2 so every call reads HBM."""
+    import torch
+    mvb = load_pkg()
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    peak, peak_kind = peaks()
+    shapes = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 1152, 4), (896, 65536, 8),
+              (896, 151936, 8), (8192, 131072, 4)]
+    if args.only:
+        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+    out_lines = []
+    for n, d, bits in shapes:
+        b = _alg_bytes(n, d, bits)
+        copies = max(2, min(4096, -(-300 * 2**20 // b)))
+        w, sc = _rand_matrix(torch, n, d, bits, copies, gen)
+        xq = torch.randint(-127, 128, (n,), dtype=torch.int8, device="cuda", generator=gen)
+        xs = torch.rand(n // 32, device="cuda", generator=gen) * 0.05
+        out = torch.empty(d, device="cuda")
+        reps = max(copies, 64)
+        t = _time_graph(torch, lambda i: mvb.matvec4(w[i % copies], sc[i % copies], xq, xs, out, n, d, bits), reps)
+        line = {"shape": f"{d}x{n} Q{bits}", "us": round(t * 1e6, 3), "GBps": round(b / t / 1e9, 1),
+                "frac": round(b / t / 1e9 / peak, 4), "bytes": b, "copies": copies,
+                "rows_per_tile": mvb.rows_per_tile(n, d)}
+        out_lines.append(line)
+        print(json.dumps(line), flush=True)
+        del w, sc
+        torch.cuda.empty_cache()
+    print(json.dumps({"mode": "sweep", "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "results": out_lines}))
+
+
+def sharded_mode(args, rank, world, local_rank):
+    """Config 5: one matrix row-sharded across the ranks (contiguous row blocks), each rank's matvec on its
+    shard, then an NCCL all-gather of the fp32 output rows so every rank holds the whole output. Timed per step
+    with CUDA events, max over ranks; the all-gather alone is timed the same way."""
+    import torch
+    import torch.distributed as dist
+    mvb = load_pkg()
+    torch.cuda.set_device(local_rank)
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    peak, peak_kind = peaks()
+    results = []
+    for n, d, bits in ((8192, 131072, 4), (896, 151936, 8)):
+        rows = -(-d // world)  # rows per rank (the last rank's block is padded with unused rows)
+        r0 = rank * rows
+        mine = max(0, min(rows, d - r0))
+        b_local = _alg_bytes(n, rows, bits)
+        copies = max(1, -(-300 * 2**20 // b_local))
+        w, sc = _rand_matrix(torch, n, rows, bits, copies, gen)
+        xq = torch.randint(-127, 128, (n,), dtype=torch.int8, device="cuda",
+                           generator=torch.Generator(device="cuda").manual_seed(7))
+        xs = torch.full((n // 32,), 0.01, device="cuda")
+        part = torch.empty(rows, device="cuda")
+        full = torch.empty(rows * world, device="cuda")
+
+        def step(i):
+            mvb.matvec4(w[i % copies], sc[i % copies], xq, xs, part, n, rows, bits)
+            dist.all_gather_into_tensor(full, part)
+
+        def gather_only(i):
+            dist.all_gather_into_tensor(full, part)
+
+        def timed(fn, k):
+            for i in range(args.warmup):
+                fn(i)
+            torch.cuda.synchronize()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(k):
+                fn(i)
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / 1000.0 / k], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        t_step = timed(step, args.steps)
+        t_ag = timed(gather_only, args.steps)
+        # correctness: this rank's block of the gathered output equals its local result
+        ok = torch.equal(full[r0:r0 + rows], part)
+        okt = torch.tensor([1 if ok else 0], device="cuda")
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+        total = _alg_bytes(n, d, bits)
+        results.append({"shape": f"{d}x{n} Q{bits}", "batch": 1, "n_gpus": world, "rows_per_gpu": rows,
+                        "us_per_step": round(t_step * 1e6, 2), "allgather_us": round(t_ag * 1e6, 2),
+                        "GBps_total": round(total / t_step / 1e9, 1),
+                        "frac_of_aggregate_hbm": round(total / t_step / 1e9 / (peak * world), 4),
+                        "gathered_ok": bool(okt.item())})
+        del w, sc
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps({"mode": "sharded", "peak_per_gpu": peak, "peak_source": f"{peak_kind} hbm_gbs",
+                          "collective": "NCCL all_gather_into_tensor", "results": results}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -277,12 +418,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default="", help="sweep: run only this shape, rows x columns (e.g. 131072x8192)")
+    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded"],
+                    help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.mode == "sweep":
+        sweep_mode(args)
         return
     if world > 1:
         import datetime
@@ -292,10 +439,20 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        our_arm(args, rank, world, local_rank)
+        if args.mode == "sharded":
+            if world == 1:
+                import datetime
+                import torch
+                import torch.distributed as dist
+                dist.init_process_group("gloo" if not torch.cuda.is_available() else "nccl", rank=0, world_size=1,
+                                        init_method="tcp://127.0.0.1:29531", timeout=datetime.timedelta(seconds=300))
+                world = 1
+            sharded_mode(args, rank, world, local_rank)
+        else:
+            our_arm(args, rank, world, local_rank)
     finally:
-        if world > 1:
-            import torch.distributed as dist
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
             dist.destroy_process_group()
 
 

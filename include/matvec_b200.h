@@ -41,6 +41,7 @@ int mvb_qmatvec(const void *wq, const void *ws, const float *x, float *out, int 
 /* Rows per CTA tile that the launchers pick for a d x n matrix (exposed for the benchmark's accounting). */
 int mvb_rows_per_tile(int n, int d);
 
+
 /* ---- Device-resident Qwen2 decode (the reference's token loop, qwen/qwen.c:490-712, on the device) ----
  * The whole forward step (embedding, per-layer rmsnorm/quantize/matvecs/attention/SwiGLU, head, greedy argmax)
  * runs on the current CUDA device as one captured CUDA graph, every matvec being this library's kernel. Token

@@ -202,6 +202,7 @@ def rows_per_tile(n, d):
     return lib().mvb_rows_per_tile(n, d)
 
 
+
 def norm_matvec4_static(x, norm_w, eps, w, ws, out, n, d, wbits, stream=None):
     """rmsnorm + quantize + matvec4 on CUDA tensors with no device allocation (scratch in a fixed device array);
     returns the C return code (0, or -1 with last_error())."""

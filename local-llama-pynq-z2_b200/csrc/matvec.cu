@@ -1,6 +1,10 @@
 // Launchers of the matvec kernels and the device-pointer entry points of include/matvec_b200.h.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
+
+#include <map>
+#include <mutex>
 
 #include "../../include/matvec_b200.h"
 #include "matvec_kernels.cuh"
@@ -27,12 +31,13 @@ const char *last_error() { return g_err; }
 int rows_per_tile(int n, int d) {
     (void)n;
     const int target_tiles = 148 * 4;
-    int rt = (d + target_tiles - 1) / target_tiles;
+    const int rt = (d + target_tiles - 1) / target_tiles;
     return rt < 1 ? 1 : (rt > 32 ? 32 : rt);
 }
 
 template <int FMT, int GS>
-static cudaError_t launch(const MatvecParams &p, cudaStream_t stream, bool pdl) {
+static cudaError_t launch(MatvecParams p, cudaStream_t stream, bool pdl) {
+    p.rt = rows_per_tile(p.n, p.d);
     const size_t smem = matvec_smem_bytes(p.n, GS, p.rt);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.d + p.rt - 1) / p.rt);
@@ -85,7 +90,6 @@ int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *w
     p.out = out;
     p.n = n;
     p.d = d;
-    p.rt = rows_per_tile(n, d);
     p.xmode = xmode;
     cudaError_t e;
     if (fmt == kQ4F16) e = launch<kQ4F16, 32>(p, stream, pdl);
@@ -138,3 +142,4 @@ extern "C" int mvb_qmatvec(const void *wq, const void *ws, const float *x, float
     return launch_matvec("mvb_qmatvec", kQ8F32, gs, wq, ws, nullptr, nullptr, x, out, n, d, kXQuantizeRunq,
                          static_cast<cudaStream_t>(stream));
 }
+

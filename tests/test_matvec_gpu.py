@@ -231,3 +231,16 @@ def test_every_fp16_scale_pattern(mvb, torch, restatement):
     out = run_matvec4(mvb, torch, w, ws, xq, xs, n, d, 4)
     ref = restatement.matvec_f16(w, ws, xq, xs, n, d, 4)
     assert same_bits(out, ref)
+
+
+@pytest.mark.parametrize("n,d,bits", [(4096, 8195, 4), (896, 65539, 8), (8192, 4100, 4)])
+def test_large_matrices_ragged(mvb, torch, restatement, n, d, bits):
+    """Large matrices with a ragged last tile: bit-exact on sampled rows, every row written."""
+    rng = np.random.default_rng(n + d)
+    w, ws = _random_q(rng, n, d, bits)
+    xq = rng.integers(-128, 128, n).astype(np.int8)
+    xs = rng.uniform(1e-3, 1e-1, n // 32).astype(np.float32)
+    out = run_matvec4(mvb, torch, w, ws, xq, xs, n, d, bits)
+    rows = np.concatenate([np.arange(40), rng.choice(d, 300, replace=False), np.arange(d - 40, d)])
+    assert same_bits(out[rows], restatement.matvec_f16(w[rows], ws[rows], xq, xs, n, rows.size, bits))
+    assert not np.isnan(out).any()
