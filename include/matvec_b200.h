@@ -120,6 +120,32 @@ int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, cons
  * /tmp). entries/thresh (may be NULL) receive the table size and probe threshold. 0, or -1. */
 int mvb_expf_eval(const float *x, float *y, int n, int *entries, float *thresh, void *stream);
 
+/* ---- Row-sharded matvec with the all-gather fused into the kernel (one process per GPU, NVLink peers) ----
+ * No counterpart in the reference, which drives one board: this is fpga_matvec4 (driver/matvec_fpga.h:29-33)
+ * for a matrix whose rows are split across `world` GPUs, rank r owning rows [r * rows, (r + 1) * rows). Each
+ * rank's kernel stores its finished rows straight into every rank's gathered output over NVLink and signals
+ * every rank's arrival counter; a bounded wait on the stream then holds back later work until all ranks' rows
+ * have arrived. No NCCL call and no peer loads.
+ *
+ * Set-up: mvb_gather_create on every rank (fills `handle`, mvb_gather_handle_size() bytes, with this rank's
+ * CUDA IPC handle), exchange the handles (any host channel), then mvb_gather_connect with all ranks' handles in
+ * rank order. Every rank must then make the same sequence of mvb_gather_matvec4 calls with the same n. */
+int mvb_gather_handle_size(void);
+void *mvb_gather_create(int rank, int world, int rows, void *handle);  /* NULL on error */
+int mvb_gather_connect(void *gather, const void *handles);            /* 0, or -1 */
+
+/* This rank's shard (rows x n, wbits 4 or 8, .qwb layout; xq/xs the full activation vector) on `stream`. The
+ * gathered output (rows * world fp32, rank-major) is mvb_gather_output's buffer once the stream reaches the
+ * next operation. The output is double-buffered: read each call's output before the call after next. 0, or -1. */
+int mvb_gather_matvec4(void *gather, const void *w, const void *ws, const void *xq, const void *xs, int n, int wbits,
+                       void *stream);
+float *mvb_gather_output(void *gather);  /* device pointer of the last call's gathered output */
+
+/* 1 if a wait gave up (some rank's rows never arrived within 2 s), 0 if none did, -1 on error; synchronizes
+ * `stream`. After a 1 the gather's counters no longer match: destroy it and create a new one on every rank. */
+int mvb_gather_error(void *gather, void *stream);
+void mvb_gather_destroy(void *gather);
+
 #ifdef __cplusplus
 }
 #endif

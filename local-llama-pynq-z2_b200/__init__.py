@@ -90,6 +90,19 @@ def lib():
         L.mvb_qwen_profile.argtypes = [vp, C.POINTER(C.c_float), i]
         L.mvb_qwen_kernel_info.restype = i
         L.mvb_qwen_kernel_info.argtypes = [vp, i, i, C.c_char_p, i, ip, C.POINTER(C.c_double)]
+        L.mvb_gather_handle_size.restype = i
+        L.mvb_gather_create.restype = vp
+        L.mvb_gather_create.argtypes = [i, i, i, vp]
+        L.mvb_gather_connect.restype = i
+        L.mvb_gather_connect.argtypes = [vp, vp]
+        L.mvb_gather_matvec4.restype = i
+        L.mvb_gather_matvec4.argtypes = [vp] * 5 + [i, i, vp]
+        L.mvb_gather_output.restype = vp
+        L.mvb_gather_output.argtypes = [vp]
+        L.mvb_gather_error.restype = i
+        L.mvb_gather_error.argtypes = [vp, vp]
+        L.mvb_gather_destroy.restype = None
+        L.mvb_gather_destroy.argtypes = [vp]
         _bind_extra(L)
         _lib = L
     return _lib
@@ -215,6 +228,70 @@ def expf_device(x, y, stream=None):
     e, t = C.c_int(), C.c_float()
     check(lib().mvb_expf_eval(_ptr(x), _ptr(y), x.numel(), C.byref(e), C.byref(t), _stream(stream)), "mvb_expf_eval")
     return e.value, t.value
+
+
+# ---- row-sharded matvec with the all-gather in the kernel (include/matvec_b200.h, mvb_gather_*) ----
+
+class _DeviceVector:
+    """A CUDA float32 vector at a device address owned by the library, for torch.as_tensor."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class ShardGather:
+    """One rank of a row-sharded matvec4 whose output rows are all-gathered inside the kernel.
+
+        g = ShardGather(rank, world, rows)
+        handles = exchange(g.handle())           # every rank's handle, in rank order (any host channel)
+        g.connect(handles)
+        g.matvec4(w_shard, ws_shard, xq, xs, n, 4)
+        full = g.output()                        # torch view, rows * world fp32, valid in stream order
+    """
+
+    def __init__(self, rank, world, rows):
+        L = lib()
+        self.rank, self.world, self.rows = rank, world, rows
+        buf = (C.c_uint8 * L.mvb_gather_handle_size())()
+        self._g = L.mvb_gather_create(rank, world, rows, buf)
+        if not self._g:
+            raise MatvecError(f"mvb_gather_create failed: {last_error()}")
+        self._handle = bytes(buf)
+
+    def handle(self):
+        return self._handle
+
+    def connect(self, handles):
+        if len(handles) != self.world:
+            raise ValueError(f"need {self.world} handles, got {len(handles)}")
+        blob = b"".join(handles)
+        check(lib().mvb_gather_connect(self._g, C.c_char_p(blob)), "mvb_gather_connect")
+
+    def matvec4(self, w, ws, xq, xs, n, wbits, stream=None):
+        return check(lib().mvb_gather_matvec4(self._g, _ptr(w), _ptr(ws), _ptr(xq), _ptr(xs), n, wbits,
+                                              _stream(stream)), "mvb_gather_matvec4")
+
+    def output(self):
+        import torch
+        ptr = lib().mvb_gather_output(self._g)
+        if not ptr:
+            raise MatvecError("no gathered output yet (call matvec4 first)")
+        return torch.as_tensor(_DeviceVector(ptr, self.rows * self.world), device="cuda")
+
+    def error(self, stream=None):
+        return lib().mvb_gather_error(self._g, _stream(stream))
+
+    def close(self):
+        if getattr(self, "_g", None):
+            lib().mvb_gather_destroy(self._g)
+            self._g = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ---- device-resident Qwen2 decode (include/matvec_b200.h, mvb_qwen_*) ----

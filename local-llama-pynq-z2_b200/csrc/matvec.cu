@@ -5,6 +5,7 @@
 
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "../../include/matvec_b200.h"
 #include "matvec_kernels.cuh"
@@ -26,21 +27,52 @@ void clear_error() { g_err[0] = 0; }
 
 const char *last_error() { return g_err; }
 
-// Rows per CTA: enough tiles for ~4 CTAs per SM on 148 SMs, at most 32 rows so the in-order fold stays one
-// warp and the product buffer stays small.
-int rows_per_tile(int n, int d) {
-    (void)n;
-    const int target_tiles = 148 * 4;
-    const int rt = (d + target_tiles - 1) / target_tiles;
-    return rt < 1 ? 1 : (rt > 32 ? 32 : rt);
+// Resident CTAs of `kernel` on the current device at kThreads threads and `smem` bytes (all SMs), cached per
+// device, kernel and size; 148 * 4 if the device cannot be queried.
+int resident_slots(const void *kernel, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, const void *, size_t>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148 * 4;
+    std::lock_guard<std::mutex> lock(mu);
+    int &slots = cache[std::make_tuple(dev, kernel, smem)];
+    if (!slots) {
+        int sms = 0, per_sm = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess ||
+            sms <= 0 || per_sm <= 0) {
+            cudaGetLastError();
+            return 148 * 4;
+        }
+        slots = sms * per_sm;
+    }
+    return slots;
 }
 
-template <int FMT, int GS>
+// Persistent row layout for d rows of n columns: one CTA per resident slot (at most one per row), each owning a
+// balanced block of rows that it streams in tiles of rt <= 32 rows (one warp folds a tile). Returns the grid.
+int row_layout(const void *kernel, int n, int gs, int d, int &rt, size_t &smem) {
+    const int slots = resident_slots(kernel, matvec_smem_bytes(n, gs, 32));
+    const int grid = d < slots ? d : slots;
+    const int per_cta = (d + grid - 1) / grid;
+    rt = per_cta < 32 ? per_cta : 32;
+    smem = matvec_smem_bytes(n, gs, rt);
+    return grid;
+}
+
+int rows_per_tile(int n, int d) {
+    int rt = 1;
+    size_t smem = 0;
+    row_layout((const void *)matvec_kernel<kQ4F16, 32, kXQuantized>, n, 32, d, rt, smem);
+    return rt;
+}
+
+template <int FMT, int GS, int XM>
 static cudaError_t launch(MatvecParams p, cudaStream_t stream, bool pdl) {
-    p.rt = rows_per_tile(p.n, p.d);
-    const size_t smem = matvec_smem_bytes(p.n, GS, p.rt);
+    size_t smem = 0;
+    const int grid = row_layout((const void *)matvec_kernel<FMT, GS, XM>, p.n, GS, p.d, p.rt, smem);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.d + p.rt - 1) / p.rt);
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -51,7 +83,7 @@ static cudaError_t launch(MatvecParams p, cudaStream_t stream, bool pdl) {
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, matvec_kernel<FMT, GS>, p);
+    return cudaLaunchKernelEx(&cfg, matvec_kernel<FMT, GS, XM>, p);
 }
 
 static bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
@@ -77,8 +109,9 @@ int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *w
                   "scales and out their element size)", who);
         return -1;
     }
-    if (!quantized && !(xmode == kXQuantizeQwen || xmode == kXQuantizeRunq)) {
-        set_error("%s: bad activation mode %d", who, xmode);
+    // The activation quantizer goes with the weight format: qwen.c's for the .qwb formats, runq.c's for runq's.
+    if (!quantized && xmode != (fmt == kQ8F32 ? kXQuantizeRunq : kXQuantizeQwen)) {
+        set_error("%s: activation mode %d does not go with weight format %d", who, xmode, fmt);
         return -1;
     }
     MatvecParams p;
@@ -92,10 +125,14 @@ int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *w
     p.d = d;
     p.xmode = xmode;
     cudaError_t e;
-    if (fmt == kQ4F16) e = launch<kQ4F16, 32>(p, stream, pdl);
-    else if (fmt == kQ8F16) e = launch<kQ8F16, 32>(p, stream, pdl);
-    else if (gs == 32) e = launch<kQ8F32, 32>(p, stream, pdl);
-    else e = launch<kQ8F32, 64>(p, stream, pdl);
+    if (fmt == kQ4F16) e = quantized ? launch<kQ4F16, 32, kXQuantized>(p, stream, pdl)
+                                     : launch<kQ4F16, 32, kXQuantizeQwen>(p, stream, pdl);
+    else if (fmt == kQ8F16) e = quantized ? launch<kQ8F16, 32, kXQuantized>(p, stream, pdl)
+                                          : launch<kQ8F16, 32, kXQuantizeQwen>(p, stream, pdl);
+    else if (gs == 32) e = quantized ? launch<kQ8F32, 32, kXQuantized>(p, stream, pdl)
+                                     : launch<kQ8F32, 32, kXQuantizeRunq>(p, stream, pdl);
+    else e = quantized ? launch<kQ8F32, 64, kXQuantized>(p, stream, pdl)
+                       : launch<kQ8F32, 64, kXQuantizeRunq>(p, stream, pdl);
     if (e != cudaSuccess) {
         set_error("%s: kernel launch failed: %s", who, cudaGetErrorString(e));
         return -1;

@@ -134,28 +134,31 @@ struct MatvecMinBlocks {
     static constexpr int value = FMT == kQ8F16 ? 5 : 4;
 };
 
-template <int FMT, int GS>
-__global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_kernel(const MatvecParams p) {
-    constexpr int GB = FMT == kQ4F16 ? GS / 2 : GS;  // weight bytes per group
-    constexpr int WC = GB / 16;                        // 16-byte weight chunks per group
-    constexpr int XC = GS / 16;                        // 16-byte activation chunks per group
-    constexpr int K = FMT == kQ4F16 ? 4 : (GS == 32 ? 2 : 1);  // groups in flight per thread
-    extern __shared__ __align__(16) uint8_t smem[];
+// Shared-memory views of one CTA (layout of matvec_smem_bytes).
+template <int GS>
+struct MatvecSmem {
+    uint4 *xplane;
+    float *xs;
+    int *xsum;
+    float *prod;
+    __device__ __forceinline__ MatvecSmem(uint8_t *smem, int ng) {
+        xplane = reinterpret_cast<uint4 *>(smem);
+        xs = reinterpret_cast<float *>(xplane + (GS / 16) * ng);
+        xsum = reinterpret_cast<int *>(xs + ng);
+        prod = reinterpret_cast<float *>(xsum + ng);
+    }
+};
 
+// Stages the activations of p (quantized, or quantized here per XM, an XMode) in shared memory: the planes, the
+// scales and (int4) the per-group sums. Ends with a barrier. XM is a template parameter so the kernels fed
+// quantized activations carry no quantize code.
+template <int FMT, int GS, int XM>
+__device__ __forceinline__ void stage_activations(const MatvecParams &p, const MatvecSmem<GS> &sm) {
+    constexpr int XC = GS / 16;  // 16-byte activation chunks per group
     const int n = p.n, ng = n / GS;
-    const int row0 = blockIdx.x * p.rt;
-    const int rows = min(p.rt, p.d - row0);
-    uint4 *xplane = reinterpret_cast<uint4 *>(smem);
-    float *xs_s = reinterpret_cast<float *>(xplane + XC * ng);
-    int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
-    float *prod = reinterpret_cast<float *>(xsum_s + ng);
     const int tid = threadIdx.x;
-
-    // The activations may come from the kernel launched just before this one.
-    wait_for_producer();
-
-    // Stage the activations in shared memory.
-    if (p.xmode == kXQuantized) {
+    uint4 *xplane = sm.xplane;
+    if (XM == kXQuantized) {
         for (int c = tid; c < n / 16; c += kThreads) {
             const uint4 a = *reinterpret_cast<const uint4 *>(p.xq + 16 * c);
             const int g = c / XC, k = c % XC;
@@ -172,11 +175,11 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_
                 xplane[k * ng + g] = a;
             }
         }
-        for (int g = tid; g < ng; g += kThreads) xs_s[g] = p.xs[g];
+        for (int g = tid; g < ng; g += kThreads) sm.xs[g] = p.xs[g];
     } else {
         for (int g = tid; g < ng; g += kThreads) {
             int8_t q[GS];
-            xs_s[g] = quantize_group<GS>(p.x, g, p.xmode, q);
+            sm.xs[g] = quantize_group<GS>(p.x, g, XM, q);
             uint32_t wv[GS / 4];
 #pragma unroll
             for (int j = 0; j < GS / 4; j++)
@@ -210,10 +213,27 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_
             s = __dp4a((int)o.y, 0x01010101, s);
             s = __dp4a((int)o.z, 0x01010101, s);
             s = __dp4a((int)o.w, 0x01010101, s);
-            xsum_s[g] = s;
+            sm.xsum[g] = s;
         }
         __syncthreads();
     }
+}
+
+// The rows [row0, row0 + rows) of p (rows <= p.rt) against the staged activations: every group's product into
+// shared memory, a barrier, then thread r adds row r's products in group order and hands the sum to
+// store(row, value) (row index within p's d rows). The caller separates consecutive tiles of one CTA with a
+// barrier.
+template <int FMT, int GS, class Store>
+__device__ __forceinline__ void stream_tile(const MatvecParams &p, const MatvecSmem<GS> &sm, int row0, int rows,
+                                            Store store) {
+    constexpr int GB = FMT == kQ4F16 ? GS / 2 : GS;  // weight bytes per group
+    constexpr int WC = GB / 16;                        // 16-byte weight chunks per group
+    constexpr int K = FMT == kQ4F16 ? 4 : (GS == 32 ? 2 : 1);  // groups in flight per thread
+    const int ng = p.n / GS;
+    const int tid = threadIdx.x;
+    const uint4 *xplane = sm.xplane;
+    const float *xs_s = sm.xs;
+    float *prod = sm.prod;
 
     // Stream this tile's groups: unit u = r*ng + g, contiguous in memory.
     const int units = rows * ng;
@@ -252,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_
                         acc = __dp4a((int)lo, (int)ev[j], acc);
                         acc = __dp4a((int)hi, (int)ov[j], acc);
                     }
-                    acc -= 8 * xsum_s[g];
+                    acc -= 8 * sm.xsum[g];
                 } else {
 #pragma unroll
                     for (int c = 0; c < WC; c++) {
@@ -280,7 +300,30 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_
         float v = 0.0f;
 #pragma unroll 8
         for (int j = 0; j < ng; j++) v = __fadd_rn(v, pr[j]);
-        p.out[row0 + tid] = v;
+        store(row0 + tid, v);
+    }
+}
+
+// Rows [r0, r1) of CTA b of a grid over d rows: contiguous, balanced to within one row.
+__device__ __forceinline__ void cta_rows(int d, int b, int grid, int &r0, int &r1) {
+    r0 = (int)((long long)d * b / grid);
+    r1 = (int)((long long)d * (b + 1) / grid);
+}
+
+// Persistent: one CTA per resident slot (or per row when d is smaller), each owning a balanced contiguous block of
+// rows that it streams in tiles of at most rt rows, with the activations staged once.
+template <int FMT, int GS, int XM>
+__global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_kernel(const MatvecParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const MatvecSmem<GS> sm(smem, p.n / GS);
+    // The activations may come from the kernel launched just before this one.
+    wait_for_producer();
+    stage_activations<FMT, GS, XM>(p, sm);
+    int r0, r1;
+    cta_rows(p.d, blockIdx.x, gridDim.x, r0, r1);
+    for (int row0 = r0; row0 < r1; row0 += p.rt) {
+        stream_tile<FMT, GS>(p, sm, row0, min(p.rt, r1 - row0), [&](int row, float v) { p.out[row] = v; });
+        __syncthreads();  // the next tile rewrites the product buffer
     }
 }
 

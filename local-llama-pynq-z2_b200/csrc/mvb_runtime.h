@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdarg.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace mvb {
@@ -15,6 +16,10 @@ void clear_error();
 int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *ws, const void *xq, const void *xs,
                   const float *x, float *out, int n, int d, int xmode, cudaStream_t stream, bool pdl = false);
 
+// Persistent row layout of a matvec kernel (matvec_kernels.cuh): returns the grid, sets the tile rows and the
+// dynamic shared memory. resident_slots: resident CTAs of a kernel over all SMs of the current device.
+int row_layout(const void *kernel, int n, int gs, int d, int &rt, size_t &smem);
+int resident_slots(const void *kernel, size_t smem);
 int rows_per_tile(int n, int d);
 
 }  // namespace mvb
