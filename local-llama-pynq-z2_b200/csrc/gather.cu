@@ -7,13 +7,14 @@
 // every tile stores its finished rows directly into every rank's gathered-output buffer (peer mappings opened
 // through CUDA IPC). Only plain stores and system-scope atomics cross NVLink: no peer loads and no NCCL call.
 //
-// The kernel is persistent (one CTA per resident slot, tiles strided over the grid) so that the costs paid once
-// per CTA -- staging the activations, the fence that publishes its rows, one count on a local counter -- are paid
-// once per slot rather than once per tile. Completion: each CTA fences its stores at GPU scope and adds 1 to this
-// rank's CTA counter; the CTA that brings it to the grid size fences at system scope (cumulatively covering every
-// CTA's stores it has synchronized with), adds 1 with release semantics to every rank's arrival counter, and then
-// holds the kernel open until its own arrival counter shows every rank's signal for this call (acquire). So when
-// the kernel ends on a rank, the whole gathered vector is in that rank's memory.
+// The kernel is persistent (one CTA per resident slot, each owning a balanced block of rows) so that the costs
+// paid once per CTA -- staging the activations, the fence that publishes its rows, one count on a local counter --
+// are paid once per slot rather than once per tile. Completion: each CTA fences its stores at GPU scope and adds 1
+// to this rank's CTA counter; the CTA that brings it to the grid size fences at system scope (cumulatively
+// covering every CTA's stores it has synchronized with), adds 1 to every rank's arrival counter (one fence, then
+// relaxed adds: together a release), and then holds the kernel open until its own arrival counter shows every
+// rank's signal for this call (acquire). So when the kernel ends on a rank, the whole gathered vector is in that
+// rank's memory.
 //
 // The gathered output is double-buffered by call parity: a rank may start call e + 1 (and write into a peer's
 // buffer) while that peer still reads the output of call e, but it cannot reach call e + 2 before the peer has
@@ -48,15 +49,22 @@ struct GatherParams {
     unsigned target;            // this rank's arrival counter once every rank has signalled this call
 };
 
-__device__ __forceinline__ void red_release_sys(unsigned *p, unsigned v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Relaxed add; the system-scope fence before the first of them makes the group a release. (A release add per
+// rank would order each add after the previous one's round trip over NVLink.)
+__device__ __forceinline__ void red_relaxed_sys(unsigned *p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+// Polling load; the wait ends with a system-scope fence, which with the load that saw the value is an acquire.
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned *p) {
     unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+
+// Fences for the release / acquire patterns (fence + relaxed access); sequential consistency is not needed.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -80,19 +88,22 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) gather_
         });
         __syncthreads();  // the next tile rewrites the product buffer
     }
-    if (threadIdx.x < 32) __threadfence();  // warp 0 stored every row of this CTA
+    if (threadIdx.x < 32) fence_acq_rel_gpu();  // warp 0 stored every row of this CTA
     __syncthreads();
     if (threadIdx.x != 0) return;
     if (atomicAdd(gp.done, 1u) != gridDim.x - 1) return;
     // The last CTA of this rank: every CTA's rows are stored. Signal every rank, then wait for all of them.
     *gp.done = 0;
-    __threadfence_system();
+    fence_acq_rel_sys();
 #pragma unroll
     for (int q = 0; q < kMaxRanks; q++)
-        if (q < gp.world) red_release_sys(gp.arrive[q], 1u);
+        if (q < gp.world) red_relaxed_sys(gp.arrive[q], 1u);
     const unsigned long long t0 = global_ns();
     for (long i = 0; i < kGatherSpin; i++) {
-        if ((int)(ld_acquire_sys(gp.arrive[gp.rank]) - gp.target) >= 0) return;
+        if ((int)(ld_relaxed_sys(gp.arrive[gp.rank]) - gp.target) >= 0) {
+            fence_acq_rel_sys();
+            return;
+        }
         if ((i & 63) == 63 && global_ns() - t0 > kGatherWaitNs) break;
     }
     atomicExch(gp.err, 1);
