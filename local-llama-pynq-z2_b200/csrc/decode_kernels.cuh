@@ -1,10 +1,11 @@
 // Kernels of the device-resident decode step (qwen_decode.cu). Every kernel:
-//   1. loads what does not depend on the previous kernel (its weight tile, into registers) and lets the next
-//      kernel launch (griddepcontrol.launch_dependents), so with programmatic dependent launch the next kernel's
-//      weight fetch overlaps this one;
-//   2. waits for the previous kernel (griddepcontrol.wait) and turns its fp32 output into this kernel's int8
-//      input in every CTA at once (rmsnorm + quantize, or quantize), reading it with L2 loads;
-//   3. computes. Two kernels also have a tail run by their last CTA to finish (an atomic counter that this CTA
+//   1. loads what does not depend on the previous kernel (its weight tile into registers, norm weights; for the
+//      attention the cached keys and values of earlier positions) before it waits for the previous kernel
+//      (griddepcontrol.wait), so with programmatic dependent launch these loads overlap the previous kernel;
+//   2. turns the previous kernel's fp32 output into this kernel's int8 input in every CTA at once (rmsnorm +
+//      quantize, or quantize), reading it with L2 loads;
+//   3. computes, letting the next kernel launch (griddepcontrol.launch_dependents) once its serial prologue is
+//      done. Two kernels also have a tail run by their last CTA to finish (an atomic counter that this CTA
 //      resets for the next step): the last layer's down projection normalizes x once for the 2,048-CTA head,
 //      and the head picks the next token.
 // The arithmetic of every step is qwen.c's, operation by operation (see qwen_decode.cu).
@@ -19,6 +20,7 @@ namespace mvb {
 namespace qwen {
 
 constexpr int kImEnd = 151645, kEndOfText = 151643;  // qwen.c:31-32
+constexpr int kMaxNormPerThread = 8;                     // rmsnorm'd vectors have at most 8 * 256 = 2048 elements
 
 struct State {
     int token;       // token of the current position
@@ -32,80 +34,46 @@ struct State {
 
 __device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 
-// ((0 + x0^2) + x1^2) + ... in order (qwen.c:339), by one thread from shared memory (n % 16 == 0, 16-byte aligned).
-// The squares are off the dependency chain and the next 16 values are loaded before the current 16 are added, so
-// the loop runs at the latency of one fp32 add per element.
-__device__ __forceinline__ float sum_squares_inorder(const float *x, int n) {
-    const float4 *x4 = reinterpret_cast<const float4 *>(x);
-    float s = 0.0f;
-    float4 c[4] = {x4[0], x4[1], x4[2], x4[3]};
-    for (int j = 0; j < n; j += 16) {
-        float4 nx[4];
-        const bool more = j + 16 < n;
-        if (more) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) nx[i] = x4[(j + 16) / 4 + i];
-        }
-        float q[16];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            q[4 * i] = __fmul_rn(c[i].x, c[i].x);
-            q[4 * i + 1] = __fmul_rn(c[i].y, c[i].y);
-            q[4 * i + 2] = __fmul_rn(c[i].z, c[i].z);
-            q[4 * i + 3] = __fmul_rn(c[i].w, c[i].w);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++) s = __fadd_rn(s, q[i]);
-        if (more) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) c[i] = nx[i];
+// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of 32 like qwen.c:355-364 into a CTA's
+// activation planes (matvec_kernels.cuh layout: for int4 weights even/odd element planes, for int8 weights chunk
+// planes) and the scales into xs. Eight threads share a group, four consecutive elements each, so one pass of the
+// CTA covers 32 groups. The group maximum is taken over the float bits of |v| (order-free and exact; NaN counts
+// as 0, since qwen.c's fmaxf ignores NaN), combined across the eight threads with three shuffles.
+template <int BITS>
+__device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs) {
+    const int ng = n / 32, l = threadIdx.x & 7;
+    for (int base = 0; base < ng; base += kThreads / 8) {  // the same trip count in every thread (shuffles)
+        const int g = base + (threadIdx.x >> 3);
+        const bool on = g < ng;
+        float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (on) f = reinterpret_cast<const float4 *>(v + 32 * g)[l];
+        auto bits = [](float x) {
+            const float a = fabsf(x);
+            return a == a ? __float_as_uint(a) : 0u;
+        };
+        unsigned m = max(max(bits(f.x), bits(f.y)), max(bits(f.z), bits(f.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        const float scale = __fmul_rn(__uint_as_float(m), 1.0f / 127.0f);
+        const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, same value
+        const uint32_t q0 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.x, inv)));
+        const uint32_t q1 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.y, inv)));
+        const uint32_t q2 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.z, inv)));
+        const uint32_t q3 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.w, inv)));
+        if (on) {
+            if (BITS == 4) {
+                // elements 4l, 4l+2 are even-plane bytes 2l, 2l+1; elements 4l+1, 4l+3 odd-plane bytes 2l, 2l+1
+                *reinterpret_cast<uint16_t *>(planes + g * 16 + 2 * l) = (uint16_t)(q0 | q2 << 8);
+                *reinterpret_cast<uint16_t *>(planes + (ng + g) * 16 + 2 * l) = (uint16_t)(q1 | q3 << 8);
+            } else {
+                // elements 4l .. 4l+3 are bytes 4(l & 3) .. of chunk l >> 2
+                *reinterpret_cast<uint32_t *>(planes + ((l >> 2) * ng + g) * 16 + 4 * (l & 3)) =
+                    q0 | q1 << 8 | q2 << 16 | q3 << 24;
+            }
+            if (l == 0) xs[g] = scale;
         }
     }
-    return s;
-}
-
-// ((0 + a0) + a1) + ... over a[0 .. n-1] in order, one thread, shared memory (any n, 16-byte aligned a).
-__device__ __forceinline__ float sum_inorder(const float *a, int n) {
-    float s = 0.0f;
-    int j = 0;
-    const float4 *a4 = reinterpret_cast<const float4 *>(a);
-    if (n >= 16) {
-        float4 c[4] = {a4[0], a4[1], a4[2], a4[3]};
-        for (; j + 16 <= n; j += 16) {
-            float4 nx[4];
-            const bool more = j + 32 <= n;
-            if (more) {
-#pragma unroll
-                for (int i = 0; i < 4; i++) nx[i] = a4[(j + 16) / 4 + i];
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                s = __fadd_rn(s, c[i].x);
-                s = __fadd_rn(s, c[i].y);
-                s = __fadd_rn(s, c[i].z);
-                s = __fadd_rn(s, c[i].w);
-            }
-            if (more) {
-#pragma unroll
-                for (int i = 0; i < 4; i++) c[i] = nx[i];
-            }
-        }
-    }
-    for (; j < n; j++) s = __fadd_rn(s, a[j]);
-    return s;
-}
-
-// One group of 32 values held in registers, quantized like qwen.c:355-364 (the operations of quantize_group's
-// qwen mode): returns the scale, q receives the int8 values.
-__device__ __forceinline__ float quantize32_qwen(const float (&v)[32], int8_t (&q)[32]) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(v[i]));
-    const float scale = __fmul_rn(amax, 1.0f / 127.0f);
-    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) q[i] = to_int8_x86(roundf(__fmul_rn(v[i], inv)));
-    return scale;
 }
 
 // Quantizes v[0 .. n-1] (shared memory) per group of 32 like qwen.c:355-364 into xq/xs (global); whole CTA.
@@ -130,11 +98,13 @@ __device__ __forceinline__ void rmsnorm_quantize(const float *xv, float *xb, con
                                                  int8_t *xq, float *xs) {
     __shared__ float s_inv;
     __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) xb[j] = __fmul_rn(xv[j], xv[j]);
+    __syncthreads();
     if (threadIdx.x == 0) {
-        float ss = sum_squares_inorder(xv, n);
+        float ss = chain_sum(xb, n);
         ss = __fdiv_rn(ss, (float)n);
         ss = __fadd_rn(ss, eps);
-        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(ss));
+        s_inv = __frcp_rn(__fsqrt_rn(ss));  // 1.0f / sqrtf(...): same value
     }
     __syncthreads();
     const float s = s_inv;
@@ -251,8 +221,20 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             hs[k] = ld_u16(sb + idx);
         }
     }
-    allow_consumer();
+    // the rmsnorm weights this thread applies (constants), also before the wait
+    float nw[kMaxNormPerThread];
+    if (PRO == kProNorm) {
+#pragma unroll
+        for (int i = 0; i < kMaxNormPerThread; i++) {
+            const int j = tid + i * kThreads;
+            nw[i] = j < n ? __ldg(p.norm_w + j) : 0.0f;
+        }
+    }
+    if (EPI == kEpiStore) allow_consumer();
     wait_for_producer();
+    // the residual's current value, loaded now so its latency overlaps the prologue
+    float old = 0.0f;
+    if (EPI == kEpiResidual && tid < rows) old = __ldcg(p.out + row0 + tid);
 
     // 2. this kernel's int8 input in shared-memory planes: from the previous kernel's int8 output, or quantized
     //    (after an rmsnorm) from its fp32 output by this CTA
@@ -260,59 +242,55 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     float *xs_s = reinterpret_cast<float *>(xplane + 2 * ng);
     int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
     float *prod = reinterpret_cast<float *>(xsum_s + ng);
-    auto put_chunk = [&](int g, int k, uint4 a) {  // 16 activation bytes (chunk k of group g) into the planes
-        if (BITS == 4) {
-            uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
-            uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
-            ev[0] = __byte_perm(a.x, a.y, 0x6420);
-            ev[1] = __byte_perm(a.z, a.w, 0x6420);
-            od[0] = __byte_perm(a.x, a.y, 0x7531);
-            od[1] = __byte_perm(a.z, a.w, 0x7531);
-        } else {
-            xplane[k * ng + g] = a;
-        }
-    };
+    const int ps = prod_stride(ng);
     if (PRO == kProQuantized) {
-        for (int c = tid; c < n / 16; c += kThreads) put_chunk(c >> 1, c & 1, __ldcg(reinterpret_cast<const uint4 *>(p.xq) + c));
+        for (int c = tid; c < n / 16; c += kThreads) {
+            const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p.xq) + c);
+            const int g = c >> 1, k = c & 1;
+            if (BITS == 4) {
+                uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
+                uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
+                ev[0] = __byte_perm(a.x, a.y, 0x6420);
+                ev[1] = __byte_perm(a.z, a.w, 0x6420);
+                od[0] = __byte_perm(a.x, a.y, 0x7531);
+                od[1] = __byte_perm(a.z, a.w, 0x7531);
+            } else {
+                xplane[k * ng + g] = a;
+            }
+        }
         for (int g = tid; g < ng; g += kThreads) xs_s[g] = __ldcg(p.xs + g);
     } else {
-        const float *src = p.src;
-        if (PRO == kProNorm) {  // x and the normalized x live after the product stage
-            float *xv = prod + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * (ng + 1);
-            xv = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(xv) + 15) & ~(uintptr_t)15);
-            for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
+        // the fp32 input (and, for an rmsnorm, its squares then the normalized values) after the product stage,
+        // addressed from the shared array itself so that every access compiles to a shared-memory load (a
+        // pointer that went through an integer cast would be generic, and the in-order sum would run at the
+        // generic load's latency)
+        const size_t stage = (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
+        float *xv = reinterpret_cast<float *>(smem + ((stage + 15) & ~(size_t)15));
+        for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
+        __syncthreads();
+        const float *qsrc = xv;
+        if (PRO == kProNorm) {  // qwen.c:337-344
+            float *xn = xv + n;
             __shared__ float s_inv;
+            for (int j = tid; j < n; j += kThreads) xn[j] = __fmul_rn(xv[j], xv[j]);
             __syncthreads();
             if (tid == 0) {
-                float ss = sum_squares_inorder(xv, n);
+                float ss = chain_sum(xn, n);
                 ss = __fdiv_rn(ss, (float)n);
                 ss = __fadd_rn(ss, p.eps);
-                s_inv = __fdiv_rn(1.0f, __fsqrt_rn(ss));
+                s_inv = __frcp_rn(__fsqrt_rn(ss));  // 1.0f / sqrtf(...): same value
             }
             __syncthreads();
             const float sc = s_inv;
-            for (int j = tid; j < n; j += kThreads) xv[n + j] = __fmul_rn(p.norm_w[j], __fmul_rn(sc, xv[j]));
-            __syncthreads();
-            src = xv + n;
-        }
-        for (int g = tid; g < ng; g += kThreads) {
-            int8_t q[32];
-            float v[32];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float4 f = PRO == kProNorm ? reinterpret_cast<const float4 *>(src + 32 * g)[i]
-                                                 : ld_cg4(src + 32 * g + 4 * i);
-                v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+            for (int i = 0; i < kMaxNormPerThread; i++) {
+                const int j = tid + i * kThreads;
+                if (j < n) xn[j] = __fmul_rn(nw[i], __fmul_rn(sc, xv[j]));
             }
-            xs_s[g] = quantize32_qwen(v, q);
-            uint32_t w[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++)
-                w[j] = (uint32_t)(uint8_t)q[4 * j] | (uint32_t)(uint8_t)q[4 * j + 1] << 8 |
-                       (uint32_t)(uint8_t)q[4 * j + 2] << 16 | (uint32_t)(uint8_t)q[4 * j + 3] << 24;
-            put_chunk(g, 0, make_uint4(w[0], w[1], w[2], w[3]));
-            put_chunk(g, 1, make_uint4(w[4], w[5], w[6], w[7]));
+            __syncthreads();
+            qsrc = xn;
         }
+        quantize_to_planes<BITS>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
     }
     __syncthreads();
     if (BITS == 4) {
@@ -360,22 +338,24 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                     acc = __dp4a((int)wv[k][c].w, (int)a.w, acc);
                 }
             }
-            prod[vr * (ng + 1) + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), scale_from_f16(hs[k])), xs_s[g]);
+            prod[vr * ps + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), scale_from_f16(hs[k])), xs_s[g]);
         }
     }
     __syncthreads();
 
+    // Let the next kernel launch now (its CTAs prefetch their weights and then wait for this one). Launched
+    // earlier, their resident CTAs slow this kernel's serial prologue (measured: 1,240 tok/s with the trigger at
+    // the top, 1,421 here). The qkv kernel (the only one that stores its output plainly) is the exception: its
+    // consumer is the 14-CTA attention, whose pre-wait loads of the cache are worth starting early.
+    if (EPI != kEpiStore) allow_consumer();
+
     // 4. in-order fold of each virtual row, epilogue
     float v = 0.0f;
-    if (tid < vrows) {
-        const float *pr = prod + tid * (ng + 1);
-#pragma unroll 8
-        for (int j = 0; j < ng; j++) v = __fadd_rn(v, pr[j]);
-    }
+    if (tid < vrows) v = chain_sum(prod + tid * ps, ng);
     if (EPI == kEpiStore) {
         if (tid < rows) p.out[row0 + tid] = v;
     } else if (EPI == kEpiResidual) {
-        if (tid < rows) p.out[row0 + tid] = __fadd_rn(__ldcg(p.out + row0 + tid), v);
+        if (tid < rows) p.out[row0 + tid] = __fadd_rn(old, v);
     } else if (EPI == kEpiSwiGLU) {
         __syncthreads();  // prod is reused for the fold values
         if (tid < vrows) prod[tid] = v;
@@ -383,7 +363,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         if (tid < rows) {
             float gv = prod[tid];
             const float u = prod[rows + tid];
-            gv = __fmul_rn(gv, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-gv, p.et))));
+            gv = __fmul_rn(gv, __frcp_rn(__fadd_rn(1.0f, expf_ref(-gv, p.et))));  // 1.0f / (...) of qwen.c
             p.out[row0 + tid] = __fmul_rn(gv, u);
         }
     } else {  // kEpiHead
@@ -436,8 +416,8 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
 inline size_t decode_smem_bytes(int n, int rt, int epi, int pro, int tail, int d) {
     const int ng = n / 32;
     const int vmax = epi == kEpiSwiGLU ? 2 * rt : rt;
-    size_t b = (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)vmax * (ng + 1) * 4;
-    if (pro == kProNorm) b = ((b + 15) & ~(size_t)15) + (size_t)2 * n * 4;
+    size_t b = (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)vmax * prod_stride(ng) * 4;
+    if (pro != kProQuantized) b = ((b + 15) & ~(size_t)15) + (size_t)(pro == kProNorm ? 2 : 1) * n * 4;
     size_t t = tail == kTailNormQuant ? (size_t)2 * d * 4 : 0;
     return b > t ? b : t;
 }
@@ -447,7 +427,7 @@ inline size_t decode_smem_bytes(int n, int rt, int epi, int pro, int tail, int d
 // this position, scores q.k / sqrt(hs) in order over the head's elements, softmax in order, weighted values in
 // order of position. The cached values of this head's kv head are staged in shared memory (cp.async, double
 // buffered in chunks of kVChunk positions) while the scores are computed. The last CTA quantizes the output.
-constexpr int kVChunk = 128;
+constexpr int kVChunk = 256;
 
 struct AttnParams {
     const float *qkv;   // raw outputs of the qkv matvec: q (dim) | k (kv_dim) | v (kv_dim)
@@ -477,6 +457,38 @@ __device__ __forceinline__ void stage_values(float *dst, const float *vcache, in
     }
 }
 
+// acc + a_0 v_0 + a_1 v_1 + ... + a_{nt-1} v_{nt-1}, added in order (v_t = vb[t * HS]). The products are off the
+// dependent chain of adds and are formed in blocks of 8 two blocks ahead, so the chain runs at the latency of one
+// fp32 add per position (the same scheme as chain_sum).
+template <int HS>
+__device__ __forceinline__ float weighted_chain(float acc, const float *a, const float *vb, int nt) {
+    int t = 0;
+    const int n8 = nt & ~7;
+    if (n8 >= 16) {
+        float p0[8], p1[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            p0[i] = __fmul_rn(a[i], vb[i * HS]);
+            p1[i] = __fmul_rn(a[8 + i], vb[(8 + i) * HS]);
+        }
+        for (; t < n8; t += 8) {
+            const int tn = t + 16 < n8 ? t + 16 : t;  // stays inside [0, n8)
+            float p2[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) p2[i] = __fmul_rn(a[tn + i], vb[(tn + i) * HS]);
+#pragma unroll
+            for (int i = 0; i < 8; i++) acc = __fadd_rn(acc, p0[i]);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                p0[i] = p1[i];
+                p1[i] = p2[i];
+            }
+        }
+    }
+    for (; t < nt; t++) acc = __fadd_rn(acc, __fmul_rn(a[t], vb[t * HS]));
+    return acc;
+}
+
 template <int HS>
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p) {
     extern __shared__ __align__(16) float asm_[];
@@ -486,13 +498,14 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
     __shared__ float red[kThreads / 32];
     __shared__ float s_max, s_sum;
     const int h = blockIdx.x, kvh = h / p.kv_mul, half = HS / 2, tid = threadIdx.x;
-    allow_consumer();
-    wait_for_producer();
+    // Everything up to the wait reads only what earlier steps wrote (the position, set by the previous step's
+    // head kernel; the cache rows of earlier positions) or constants (RoPE table, biases). Within one step no
+    // kernel writes them before this kernel has finished, so they are read before the qkv kernel completes.
     const int pos = __ldcg(&p.st->pos);
     const int nchunks = (pos + kVChunk - 1) / kVChunk;  // cached positions 0 .. pos-1
     if (nchunks > 0) stage_values<HS>(vbuf, p.vcache, p.kv_dim, kvh, 0, min(kVChunk, pos));
     cp_async_commit();
-    // this thread's first cached key row, loaded before the rope so both round trips overlap
+    // this thread's first cached key row
     float4 k4[HS / 4];
     if (tid < pos) {
         const float *kt = p.kcache + (size_t)tid * p.kv_dim + kvh * HS;
@@ -500,19 +513,29 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         for (int i = 0; i < HS / 4; i++) k4[i] = ld_cg4(kt + 4 * i);
     }
     const float *cs = p.rope + (size_t)pos * HS;
+    float rc = 0.0f, rs = 0.0f, bq0 = 0.0f, bq1 = 0.0f, bk0 = 0.0f, bk1 = 0.0f, bv0 = 0.0f;
+    if (tid < half) {
+        rc = cs[tid];
+        rs = cs[half + tid];
+        bq0 = p.bq[h * HS + tid];
+        bq1 = p.bq[h * HS + tid + half];
+        bk0 = p.bk[kvh * HS + tid];
+        bk1 = p.bk[kvh * HS + tid + half];
+    }
+    if (tid < HS) bv0 = p.bv[kvh * HS + tid];
+    wait_for_producer();
     const float *qr = p.qkv + h * HS, *kr = p.qkv + p.dim + kvh * HS, *vr = p.qkv + p.dim + p.kv_dim + kvh * HS;
     if (tid < half) {
-        const float c = cs[tid], s = cs[half + tid];
-        float a = __fadd_rn(__ldcg(qr + tid), p.bq[h * HS + tid]);
-        float b = __fadd_rn(__ldcg(qr + tid + half), p.bq[h * HS + tid + half]);
-        q[tid] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        q[tid + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-        a = __fadd_rn(__ldcg(kr + tid), p.bk[kvh * HS + tid]);
-        b = __fadd_rn(__ldcg(kr + tid + half), p.bk[kvh * HS + tid + half]);
-        kc[tid] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        kc[tid + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+        float a = __fadd_rn(__ldcg(qr + tid), bq0);
+        float b = __fadd_rn(__ldcg(qr + tid + half), bq1);
+        q[tid] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
+        q[tid + half] = __fadd_rn(__fmul_rn(b, rc), __fmul_rn(a, rs));
+        a = __fadd_rn(__ldcg(kr + tid), bk0);
+        b = __fadd_rn(__ldcg(kr + tid + half), bk1);
+        kc[tid] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
+        kc[tid + half] = __fadd_rn(__fmul_rn(b, rc), __fmul_rn(a, rs));
     }
-    if (tid < HS) vc[tid] = __fadd_rn(__ldcg(vr + tid), p.bv[kvh * HS + tid]);
+    if (tid < HS) vc[tid] = __fadd_rn(__ldcg(vr + tid), bv0);
     __syncthreads();
     if (h % p.kv_mul == 0 && tid < HS) {  // one writer per kv head
         p.kcache[(size_t)pos * p.kv_dim + kvh * HS + tid] = kc[tid];
@@ -556,10 +579,11 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
     const float mx = s_max;
     for (int t = tid; t <= pos; t += kThreads) att[t] = expf_ref(__fsub_rn(att[t], mx), p.et);
     __syncthreads();
-    if (tid == 0) s_sum = sum_inorder(att, pos + 1);
+    if (tid == 0) s_sum = chain_sum(att, pos + 1);
     __syncthreads();
     const float sum = s_sum;
     for (int t = tid; t <= pos; t += kThreads) att[t] = __fdiv_rn(att[t], sum);
+    allow_consumer();  // the next kernel may launch (see decode_matvec_kernel)
     // weighted values, in order of position, from the staged chunks
     float acc = 0.0f;
     for (int c = 0; c < nchunks; c++) {
@@ -571,10 +595,8 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         cp_async_wait<1>();
         __syncthreads();
         if (tid < HS) {
-            const float *vb = vbuf + (c & 1) * kVChunk * HS + tid;
-            const int t0 = c * kVChunk, nt = min(kVChunk, pos - t0);
-#pragma unroll 8
-            for (int t = 0; t < nt; t++) acc = __fadd_rn(acc, __fmul_rn(att[t0 + t], vb[t * HS]));
+            const int t0 = c * kVChunk;
+            acc = weighted_chain<HS>(acc, att + t0, vbuf + (c & 1) * kVChunk * HS + tid, min(kVChunk, pos - t0));
         }
         __syncthreads();
     }

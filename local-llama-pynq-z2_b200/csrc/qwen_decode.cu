@@ -66,7 +66,7 @@ __device__ void rmsnorm_smem(float *o, float *sq, const float *x, const float *w
         for (; j < n; j++) ss = __fadd_rn(ss, sq[j]);
         ss = __fdiv_rn(ss, (float)n);
         ss = __fadd_rn(ss, eps);
-        inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(ss));
+        inv_rms = __frcp_rn(__fsqrt_rn(ss));  // 1.0f / sqrtf(...): the correctly rounded reciprocal
     }
     __syncthreads();
     const float s = inv_rms;
