@@ -120,6 +120,20 @@ int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, cons
  * /tmp). entries/thresh (may be NULL) receive the table size and probe threshold. 0, or -1. */
 int mvb_expf_eval(const float *x, float *y, int n, int *entries, float *thresh, void *stream);
 
+/* ---- Batched prefill matmul on the tensor cores ----
+ * No counterpart in the reference, which prefills token by token (qwen.c:674-681). m tokens through one matrix
+ * at once: out[t * d + i] is fpga_matvec4's result for token t and row i, bit-identical to m separate matvecs.
+ * w (d rows, n*wbits/8 bytes each, .qwb layout), ws (d * n/32 fp16), xq (m x n int8, token-major), xs (n/32 x ldx
+ * fp32, group-major: xs[g * ldx + t] is token t's scale of group g; ldx >= m, ldx % 4 == 0), out (m x d fp32).
+ * wbits 4 or 8, n % 32 == 0, n <= 8192; w, xq and xs 16-byte aligned. Device pointers, asynchronous on `stream`.
+ * 0, or -1 with the reason in mvb_last_error(). */
+int mvb_gemm4(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m, int ldx,
+              int wbits, void *stream);
+
+/* Synchronizes `stream`; returns 0 if every GEMM kernel so far completed normally, or the code of the first
+ * internal wait that gave up (the kernel then wrote no output), and clears it; -1 if the stream failed. */
+int mvb_gemm_status(void *stream);
+
 /* ---- Row-sharded matvec with the all-gather fused into the kernel (one process per GPU, NVLink peers) ----
  * No counterpart in the reference, which drives one board: this is fpga_matvec4 (driver/matvec_fpga.h:29-33)
  * for a matrix whose rows are split across `world` GPUs, rank r owning rows [r * rows, (r + 1) * rows). Each

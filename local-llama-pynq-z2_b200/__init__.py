@@ -90,6 +90,10 @@ def lib():
         L.mvb_qwen_profile.argtypes = [vp, C.POINTER(C.c_float), i]
         L.mvb_qwen_kernel_info.restype = i
         L.mvb_qwen_kernel_info.argtypes = [vp, i, i, C.c_char_p, i, ip, C.POINTER(C.c_double)]
+        L.mvb_gemm4.restype = i
+        L.mvb_gemm4.argtypes = [vp] * 5 + [i] * 5 + [vp]
+        L.mvb_gemm_status.restype = i
+        L.mvb_gemm_status.argtypes = [vp]
         L.mvb_gather_handle_size.restype = i
         L.mvb_gather_create.restype = vp
         L.mvb_gather_create.argtypes = [i, i, i, vp]
@@ -228,6 +232,18 @@ def expf_device(x, y, stream=None):
     e, t = C.c_int(), C.c_float()
     check(lib().mvb_expf_eval(_ptr(x), _ptr(y), x.numel(), C.byref(e), C.byref(t), _stream(stream)), "mvb_expf_eval")
     return e.value, t.value
+
+
+def gemm4(w, ws, xq, xs, out, n, d, m, ldx, wbits, stream=None):
+    """m tokens through one matrix on the tensor cores (mvb_gemm4): out[t, i] = matvec4 of token t, row i.
+    xq: (m, n) int8; xs: (n/32, ldx) fp32 group-major; out: (m, d) fp32 (CUDA tensors, asynchronous)."""
+    return check(lib().mvb_gemm4(_ptr(w), _ptr(ws), _ptr(xq), _ptr(xs), _ptr(out), n, d, m, ldx, wbits,
+                                 _stream(stream)), "mvb_gemm4")
+
+
+def gemm_status(stream=None):
+    """Synchronizes and returns the GEMM kernels' error word (0 = every internal wait completed)."""
+    return lib().mvb_gemm_status(_stream(stream))
 
 
 # ---- row-sharded matvec with the all-gather in the kernel (include/matvec_b200.h, mvb_gather_*) ----

@@ -1,0 +1,463 @@
+// Batched prefill matmul on the 5th-generation tensor cores: M tokens at once through one quantized matrix.
+//
+// The reference prefills its prompt one token at a time through fpga_matvec4 (qwen.c:674-681); this computes
+// the same M matvecs as one GEMM, out[m][i] = matvec of token m against row i, bit-identical to the reference
+// C path for every token (qwen.c:436-456):
+//     isum_g = sum_{k<32} w[i, 32g+k] * xq[m, 32g+k]               int32, exact
+//     out    = ((0 + fl(fl(isum_0 * ws[i,0]) * xs[m,0])) + ...)    fp32, groups in order
+// One group of 32 is exactly one K=32 step of tcgen05.mma.kind::i8, so the tensor cores produce each group's
+// int32 sum for a 128-row x BN-token tile into tensor memory, and the epilogue warps apply the two rounded
+// scale multiplies and the in-order add per group in fp32 registers.
+//
+// CTA = 128 weight rows x BN tokens; K is walked in blocks of 128 bytes (4 groups). Warp roles (320 threads):
+//   warp 0   TMA producer: the weight tile (int8, or packed int4) and the token tile per k-block into a ring
+//            of shared-memory stages (128-byte swizzled, the layout the MMA descriptors describe). For int4
+//            weights its 32 lanes then unpack the packed tile into the int8 operand tile (same swizzle).
+//   warp 1   allocates tensor memory and issues the MMAs (one thread): per group, D[buffer] = A_g x B_g^T into
+//            a ring of 4 TMEM buffers of BN columns, committed to that buffer's barrier; after a k-block's four
+//            groups a commit frees the shared-memory stage.
+//   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. Per
+//            group: tcgen05.ld of the int32 sums, release the buffer, then per column
+//            acc += fl(fl((float)isum * ws) * xs). (float)isum * ws is one fma on a biased integer: with
+//            v = bits(isum + 0x4B400000) = 12582912 + isum (exact for |isum| < 2^22), fma(v, ws, -12582912 * ws)
+//            rounds (v - 12582912) * ws = isum * ws once, and -12582912 * ws is exact because ws has at most 11
+//            significant bits (an fp16 value).
+// Every mbarrier wait is bounded (kGemmWaitNs of %globaltimer); a wait that runs out records an error, the
+// roles stop, outstanding copies and MMAs are waited for (bounded), tensor memory is freed and the kernel ends.
+// No TMA multicast; no clusters.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/matvec_b200.h"
+#include "matvec_kernels.cuh"
+#include "mvb_runtime.h"
+
+namespace mvb {
+namespace gemm {
+
+constexpr int kBM = 128;          // weight rows per CTA (MMA M)
+constexpr int kBK = 128;          // int8 K bytes per stage (4 groups)
+constexpr int kStages = 4;
+constexpr int kTmemBufs = 4;      // group accumulators in flight
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr unsigned long long kGemmWaitNs = 1000000000ull;
+
+// error codes in the error word (first failure wins)
+enum : int { kErrNone = 0, kErrFullWait = 1, kErrEmptyWait = 2, kErrTmemFull = 3, kErrTmemEmpty = 4, kErrRaw = 5 };
+
+__device__ int g_gemm_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long now_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Waits for the phase with the given parity to complete; false after kGemmWaitNs (the error is recorded).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int err) {
+    const uint32_t a = smem_u32(bar);
+    unsigned long long t0 = 0;
+    for (uint32_t i = 0;; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 1023) == 1023) {
+            const unsigned long long t = now_ns();
+            if (!t0) t0 = t;
+            else if (t - t0 > kGemmWaitNs) {
+                atomicCAS(&g_gemm_error, kErrNone, err);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ bool failed() { return *(volatile int *)&g_gemm_error != kErrNone; }
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte swizzled canonical layout: rows of 128
+// bytes, 8-row atoms of 1024 bytes one after another (stride byte offset 1024), leading byte offset 16 (unused for
+// this layout), descriptor version 1, layout type 2 (SWIZZLE_128B). Field positions as in the sm100 descriptor
+// definition (start >> 4 in bits 0-13, LBO >> 4 in 16-29, SBO >> 4 in 32-45, version in 46-47, layout in 61-63).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+           ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of tcgen05.mma.kind::i8: D s32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 =
+// 1), both K-major, N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// int4 nibbles of one 32-bit word (8 elements, element 2i in the low nibble of byte i) -> 8 int8 values as two
+// words in element order. Sign extension per byte: v | ((v & 8) * 0x1E) maps 8..15 to -8..-1 (0xF8..0xFF) without
+// carries between bytes.
+__device__ __forceinline__ uint2 unpack_int4(uint32_t w) {
+    uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+    lo |= (lo & 0x08080808u) * 0x1Eu;
+    hi |= (hi & 0x08080808u) * 0x1Eu;
+    return make_uint2(__byte_perm(lo, hi, 0x5140), __byte_perm(lo, hi, 0x7362));
+}
+
+struct GemmParams {
+    const uint16_t *ws;  // d x ng fp16 weight scales
+    const float *xs;     // ng x ldx fp32 token scales, group-major
+    float *out;          // m x d fp32, token-major
+    int n, d, m, ldx, ng;
+};
+
+template <int BN, int BITS>
+struct Smem {
+    static constexpr int kA = kBM * kBK;                    // int8 operand tile
+    static constexpr int kB = BN * kBK;                     // token tile
+    static constexpr int kRaw = BITS == 4 ? kBM * kBK / 2 : 0;  // packed int4 staging
+    static constexpr int kStage = kA + kB + kRaw;           // multiple of 1024
+    static constexpr size_t kBytes = (size_t)kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+};
+
+template <int BN, int BITS>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+    using S = Smem<BN, BITS>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * S::kStage);
+    uint64_t *full = bar, *empty = bar + kStages, *ready = bar + 2 * kStages, *tfull = bar + 3 * kStages,
+             *tempty = tfull + kTmemBufs;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + kTmemBufs);
+    constexpr int kCols = kTmemBufs * BN < 32 ? 32 : kTmemBufs * BN;  // power of two >= 32
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * kBM, m0 = blockIdx.y * BN;
+    const int nkb = (p.n + kBK - 1) / kBK;
+    const int ngroups = p.ng;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&ready[s], 1);
+        }
+        for (int j = 0; j < kTmemBufs; j++) {
+            mbar_init(&tfull[j], 1);
+            mbar_init(&tempty[j], kEpiWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto stage_a = [&](int s) { return smem + (size_t)s * S::kStage; };
+    auto stage_b = [&](int s) { return smem + (size_t)s * S::kStage + S::kA; };
+    auto stage_raw = [&](int s) { return smem + (size_t)s * S::kStage + S::kA + S::kB; };
+    constexpr uint32_t kTx = (BITS == 4 ? kBM * kBK / 2 : kBM * kBK) + BN * kBK;
+
+    if (warp == 0) {
+        // ---------------- producer (and int4 unpacker) ----------------
+        int issued = 0;  // k-blocks whose loads were issued
+        auto issue = [&](int kb) -> bool {
+            const int s = kb % kStages;
+            if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, kErrEmptyWait)) return false;
+            if (lane == 0) {
+                mbar_expect_tx(&full[s], kTx);
+                if (BITS == 4) tma_load_2d(stage_raw(s), &map_a, &full[s], kb * (kBK / 2), row0);
+                else tma_load_2d(stage_a(s), &map_a, &full[s], kb * kBK, row0);
+                tma_load_2d(stage_b(s), &map_b, &full[s], kb * kBK, m0);
+            }
+            __syncwarp();
+            return true;
+        };
+        bool ok = true;
+        for (int kb = 0; kb < nkb && kb < kStages - 1 && ok; kb++) ok = issue(kb) && ++issued;
+        for (int kb = 0; kb < nkb && ok; kb++) {
+            if (kb + kStages - 1 < nkb) {
+                ok = issue(kb + kStages - 1);
+                if (!ok) break;
+                issued++;
+            }
+            if (BITS == 4) {
+                const int s = kb % kStages;
+                if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrRaw)) { ok = false; break; }
+                // packed [128 rows][64 bytes] -> int8 [128 rows][128 bytes], 16-byte chunk c of row r stored at
+                // chunk c ^ (r & 7) (the 128-byte swizzle the TMA applies to the int8 tiles)
+                const uint8_t *raw = stage_raw(s);
+                uint8_t *a = stage_a(s);
+#pragma unroll 4
+                for (int it = 0; it < kBM / 4; it++) {
+                    const int r = it * 4 + (lane >> 3), c = lane & 7;
+                    const uint2 pk = *reinterpret_cast<const uint2 *>(raw + r * (kBK / 2) + c * 8);
+                    const uint2 e0 = unpack_int4(pk.x), e1 = unpack_int4(pk.y);
+                    *reinterpret_cast<uint4 *>(a + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
+                        make_uint4(e0.x, e0.y, e1.x, e1.y);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready[s]);
+            }
+        }
+        // copies still in flight land before the CTA can end: wait (bounded) for the last phase of each stage
+        for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; kb++)
+            mbar_wait(&full[kb % kStages], (kb / kStages) & 1, kErrFullWait);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        const uint32_t idesc = idesc_i8(kBM, BN);
+        bool ok = true;
+        int t = 0;  // group index over the whole K
+        for (int kb = 0; kb < nkb && ok; kb++) {
+            const int s = kb % kStages;
+            if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrFullWait)) break;
+            if (BITS == 4 && !mbar_wait(&ready[s], (kb / kStages) & 1, kErrRaw)) break;
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(stage_a(s)), b0 = smem_u32(stage_b(s));
+            for (int k = 0; k < kBK / 32 && t < ngroups; k++, t++) {
+                const int j = t % kTmemBufs;
+                if (t >= kTmemBufs && !mbar_wait(&tempty[j], ((t / kTmemBufs) - 1) & 1, kErrTmemEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    mma_i8(tmem + j * BN, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc);
+                    mma_commit(&tfull[j]);
+                }
+                __syncwarp();
+            }
+            if (lane == 0) mma_commit(&empty[s]);
+            __syncwarp();
+        }
+        // all MMAs complete before tensor memory is freed: wait (bounded) for the last commit
+        if (t > 0) mbar_wait(&tfull[(t - 1) % kTmemBufs], ((t - 1) / kTmemBufs) & 1, kErrTmemFull);
+    } else {
+        // ---------------- epilogue ----------------
+        constexpr int kCw = BN / 2;  // columns per thread
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        const int row = row0 + q * 32 + lane;
+        const int col0 = half * kCw;
+        float acc[kCw];
+#pragma unroll
+        for (int c = 0; c < kCw; c++) acc[c] = 0.0f;
+        const uint16_t *wsr = p.ws + (size_t)(row < p.d ? row : 0) * p.ng;
+        for (int t = 0; t < ngroups; t++) {
+            const int j = t % kTmemBufs;
+            // this row's scale of the group, loaded while the MMA runs
+            const float wsc = scale_from_f16(__ldg(wsr + t));
+            const float ncw = __fmul_rn(-12582912.0f, wsc);  // exact: wsc has <= 11 significant bits
+            const float *xsg = p.xs + (size_t)t * p.ldx + m0 + col0;
+            if (!mbar_wait(&tfull[j], (t / kTmemBufs) & 1, kErrTmemFull)) break;
+            tc_fence_after();
+            int isum[kCw];
+#pragma unroll
+            for (int c = 0; c < kCw; c += 8) {
+                int r8[8];
+                tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + j * BN + col0 + c, r8);
+#pragma unroll
+                for (int i = 0; i < 8; i++) isum[c + i] = r8[i];
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[j]);
+#pragma unroll
+            for (int c = 0; c < kCw; c += 4) {
+                // the tokens' scales of this group (the same address in every lane: one broadcast load)
+                float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (m0 + col0 + c < p.m) x4 = __ldg(reinterpret_cast<const float4 *>(xsg + c));
+                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float v = __int_as_float(isum[c + i] + 0x4B400000);
+                    const float pw = __fmaf_rn(v, wsc, ncw);  // fl(isum * ws)
+                    acc[c + i] = __fadd_rn(acc[c + i], __fmul_rn(pw, xv[i]));
+                }
+            }
+        }
+        if (!failed() && row < p.d) {
+#pragma unroll
+            for (int c = 0; c < kCw; c++)
+                if (m0 + col0 + c < p.m) p.out[(size_t)(m0 + col0 + c) * p.d + row] = acc[c];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// host side: tensor maps through the driver entry point (no link against the driver library)
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D uint8 tensor map over rows x cols bytes (row pitch cols), box box_rows x box_cols, optional 128B swizzle.
+static bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                     uint32_t box_rows, bool swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int BITS>
+static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, const GemmParams &p, cudaStream_t s) {
+    const size_t smem = Smem<BN, BITS>::kBytes;
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((p.d + kBM - 1) / kBM, (p.m + BN - 1) / BN);
+    gemm_kernel<BN, BITS><<<grid, kThreads, smem, s>>>(ma, mb, p);
+    return cudaGetLastError();
+}
+
+}  // namespace gemm
+}  // namespace mvb
+
+using namespace mvb;
+using namespace mvb::gemm;
+
+extern "C" int mvb_gemm4(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m,
+                         int ldx, int wbits, void *stream) {
+    if (wbits != 4 && wbits != 8) {
+        set_error("mvb_gemm4: unsupported wbits=%d (need 4 or 8)", wbits);
+        return -1;
+    }
+    if (n <= 0 || n % 32 || n > kMaxN || d <= 0 || m <= 0 || ldx < m || ldx % 4) {
+        set_error("mvb_gemm4: unsupported n=%d d=%d m=%d ldx=%d (need n %% 32 == 0, n <= %d, d, m >= 1, ldx >= m, "
+                  "ldx %% 4 == 0)", n, d, m, ldx, kMaxN);
+        return -1;
+    }
+    if (!w || !ws || !xq || !xs || !out || ((uintptr_t)w & 15) || ((uintptr_t)xq & 15) || ((uintptr_t)ws & 1) ||
+        ((uintptr_t)xs & 15) || ((uintptr_t)out & 3)) {
+        set_error("mvb_gemm4: null or misaligned pointer (w and xq 16 bytes, xs 16, ws 2, out 4)");
+        return -1;
+    }
+    CUtensorMap ma, mb;
+    const bool ok_a = wbits == 4 ? make_map(&ma, w, (uint64_t)n / 2, (uint64_t)d, kBK / 2, kBM, false)
+                                 : make_map(&ma, w, (uint64_t)n, (uint64_t)d, kBK, kBM, true);
+    // the token tile's box height is the instantiation's BN; chosen below
+    GemmParams p;
+    p.ws = static_cast<const uint16_t *>(ws);
+    p.xs = xs;
+    p.out = out;
+    p.n = n;
+    p.d = d;
+    p.m = m;
+    p.ldx = ldx;
+    p.ng = n / 32;
+    const int bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+    const bool ok_b = make_map(&mb, xq, (uint64_t)n, (uint64_t)m, kBK, bn, true);
+    if (!ok_a || !ok_b) {
+        set_error("mvb_gemm4: cannot build the TMA descriptors (driver entry point missing or bad layout)");
+        return -1;
+    }
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (wbits == 4) {
+        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, p, s) : bn == 32 ? launch_gemm<32, 4>(ma, mb, p, s)
+          : bn == 64 ? launch_gemm<64, 4>(ma, mb, p, s) : launch_gemm<128, 4>(ma, mb, p, s);
+    } else {
+        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, p, s) : bn == 32 ? launch_gemm<32, 8>(ma, mb, p, s)
+          : bn == 64 ? launch_gemm<64, 8>(ma, mb, p, s) : launch_gemm<128, 8>(ma, mb, p, s);
+    }
+    if (e != cudaSuccess) {
+        set_error("mvb_gemm4: launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+// Synchronizes `stream` and returns (and clears) the device error word of the GEMM kernels: 0, or the code of the
+// first wait that ran out; -1 if the stream itself failed.
+extern "C" int mvb_gemm_status(void *stream) {
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaStreamSynchronize(s) != cudaSuccess) return -1;
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof v) != cudaSuccess) return -1;
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_gemm_error, &z, sizeof z);
+    }
+    return v;
+}
