@@ -345,6 +345,69 @@ def sweep_mode(args):
     print(json.dumps({"mode": "sweep", "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "results": out_lines}))
 
 
+def prefill_mode(args):
+    """Config 4's batched part: the tensor-core prefill matmul (mvb_gemm4) with M = 16, 128 and 512 tokens on the
+    Qwen2.5-0.5B layer shapes and the Q8 head, beside the same tokens as M calls of the matvec kernel (one per
+    token, as the reference prefills). Weights rotate through copies larger than 2x L2. Reported per shape and M:
+    us per call, int8 tensor ops 2*M*d*n per second against the int8 dense rate taken as twice the measured bf16
+    peak (B200's int8 rate is twice its bf16 rate), weight GB/s, and the epilogue's rate of group results
+    (M*d*n/32 per second); `same` says the GEMM's output equals the M matvecs' bit for bit."""
+    import torch
+    mvb = load_pkg()
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    peak, peak_kind = peaks()
+    bf16 = 1590.0
+    mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(mp):
+        bf16 = float(json.load(open(mp)).get("bf16_tflops", bf16))
+    int8_peak = 2 * bf16
+    shapes = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 65536, 8)]
+    if args.only:
+        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+    out_lines = []
+    for n, d, bits in shapes:
+        wb = d * n * bits // 8 + d * (n // 32) * 2
+        copies = max(2, min(4096, -(-300 * 2**20 // wb)))
+        w, sc = _rand_matrix(torch, n, d, bits, copies, gen)
+        for m in (16, 128, 512):
+            xq = torch.randint(-127, 128, (m, n), dtype=torch.int8, device="cuda", generator=gen)
+            ldx = (m + 3) // 4 * 4
+            xs = torch.rand((n // 32, ldx), device="cuda", generator=gen) * 0.05
+            out = torch.empty((m, d), device="cuda")
+            reps = max(min(copies, 256), 16)
+            t = _time_graph(torch, lambda i: mvb.gemm4(w[i % copies], sc[i % copies], xq, xs, out, n, d, m, ldx, bits),
+                            reps)
+            status = mvb.gemm_status()
+            # the same tokens, one matvec call each
+            xs_tok = xs[:, :m].t().contiguous()
+            out_mv = torch.empty((m, d), device="cuda")
+            mv_reps = max(1, min(copies, 4096 // m))
+
+            def per_token(i):
+                for tk in range(m):
+                    mvb.matvec4(w[i % copies], sc[i % copies], xq[tk], xs_tok[tk], out_mv[tk], n, d, bits)
+
+            t_mv = _time_graph(torch, per_token, mv_reps) if m <= 128 else None
+            mvb.gemm4(w[0], sc[0], xq, xs, out, n, d, m, ldx, bits)
+            per_token(0) if m <= 128 else None
+            torch.cuda.synchronize()
+            same = bool(torch.equal(out.view(torch.int32), out_mv.view(torch.int32))) if m <= 128 else None
+            ops = 2.0 * m * d * n
+            line = {"shape": f"{d}x{n} Q{bits}", "M": m, "us": round(t * 1e6, 2),
+                    "TOPS": round(ops / t / 1e12, 1), "frac_int8": round(ops / t / 1e12 / int8_peak, 4),
+                    "weight_GBps": round(wb / t / 1e9, 1), "group_results_per_s": round(m * d * (n // 32) / t / 1e12, 3),
+                    "matvecs_us": round(t_mv * 1e6, 2) if t_mv else None,
+                    "speedup_vs_matvecs": round(t_mv / t, 1) if t_mv else None, "same": same, "status": status}
+            out_lines.append(line)
+            print(json.dumps(line), flush=True)
+        del w, sc
+        torch.cuda.empty_cache()
+    print(json.dumps({"mode": "prefill", "int8_peak_TOPS": int8_peak,
+                      "peak_source": f"2 x {peak_kind} bf16_tflops" if os.path.exists(mp) else "2 x fallback bf16",
+                      "results": out_lines}))
+
+
 def sharded_mode(args, rank, world, local_rank):
     """Config 5: one matrix row-sharded across the ranks (contiguous row blocks), each rank's matvec on its
     shard, and every rank ends the step holding the whole fp32 output. Two ways are timed per step with CUDA
@@ -441,8 +504,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="sweep: run only this shape, rows x columns (e.g. 131072x8192)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded"],
-                    help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec)")
+    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill"],
+                    help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "
+                         "prefill (tensor-core matmul over many tokens)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -452,6 +516,9 @@ def main():
         return
     if args.mode == "sweep":
         sweep_mode(args)
+        return
+    if args.mode == "prefill":
+        prefill_mode(args)
         return
     if world > 1:
         import datetime

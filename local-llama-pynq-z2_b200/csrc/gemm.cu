@@ -10,12 +10,14 @@
 // scale multiplies and the in-order add per group in fp32 registers.
 //
 // CTA = 128 weight rows x BN tokens; K is walked in blocks of 128 bytes (4 groups). Warp roles (320 threads):
-//   warp 0   TMA producer: the weight tile (int8, or packed int4) and the token tile per k-block into a ring
-//            of shared-memory stages (128-byte swizzled, the layout the MMA descriptors describe). For int4
-//            weights its 32 lanes then unpack the packed tile into the int8 operand tile (same swizzle).
-//   warp 1   allocates tensor memory and issues the MMAs (one thread): per group, D[buffer] = A_g x B_g^T into
-//            a ring of 4 TMEM buffers of BN columns, committed to that buffer's barrier; after a k-block's four
-//            groups a commit frees the shared-memory stage.
+//   warp 0   TMA producer (one thread): per k-block the weight tile (int8, or packed int4), the token tile
+//            (both 128-byte swizzled, the layout the MMA descriptors describe) and the tokens' scales of the
+//            block's four groups into a ring of shared-memory stages.
+//   warp 1   allocates tensor memory; for int4 weights its 32 lanes unpack each packed tile into the int8
+//            operand tile (same swizzle); one thread issues the MMAs: per group, D[buffer] = A_g x B_g^T into a
+//            ring of 4 TMEM buffers of BN columns, committed to that buffer's barrier. MMAs run asynchronously,
+//            so the next tile's unpack overlaps them. A stage is free once its MMAs completed (a commit) and
+//            every epilogue warp has read its token scales.
 //   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. Per
 //            group: tcgen05.ld of the int32 sums, release the buffer, then per column
 //            acc += fl(fl((float)isum * ws) * xs). (float)isum * ws is one fma on a biased integer: with
@@ -42,7 +44,6 @@ namespace gemm {
 constexpr int kBM = 128;          // weight rows per CTA (MMA M)
 constexpr int kBK = 128;          // int8 K bytes per stage (4 groups)
 constexpr int kStages = 4;
-constexpr int kTmemBufs = 4;      // group accumulators in flight
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr unsigned long long kGemmWaitNs = 1000000000ull;
@@ -165,26 +166,81 @@ struct GemmParams {
     int n, d, m, ldx, ng;
 };
 
+// N consecutive 32-bit TMEM columns (N = 8, 16 or 32) of this thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, int (&r)[N]) {
+    if constexpr (N == 8) {
+        tmem_ld8(taddr, r);
+    } else if constexpr (N == 16) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+            "%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+    } else {
+        static_assert(N == 32, "8, 16 or 32 columns");
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+            "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+              "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+    }
+}
+
+// One shared-memory stage: the int8 weight tile, the token tile, the packed int4 weight tile (int4 only) and the
+// tokens' scales of the k-block's four groups ([4][BN] fp32).
 template <int BN, int BITS>
 struct Smem {
-    static constexpr int kA = kBM * kBK;                    // int8 operand tile
-    static constexpr int kB = BN * kBK;                     // token tile
-    static constexpr int kRaw = BITS == 4 ? kBM * kBK / 2 : 0;  // packed int4 staging
-    static constexpr int kStage = kA + kB + kRaw;           // multiple of 1024
-    static constexpr size_t kBytes = (size_t)kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+    static constexpr int kA = kBM * kBK;                        // int8 operand tile (1024-aligned)
+    static constexpr int kB = BN * kBK;                         // token tile (1024-aligned)
+    static constexpr int kRaw = BITS == 4 ? kBM * kBK / 2 : 0;  // packed int4 tile
+    static constexpr int kX = 4 * BN * 4;                       // token scales
+    static constexpr int kStage = (kA + kB + kRaw + kX + 1023) / 1024 * 1024;
+    static constexpr size_t kNatural = (size_t)kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+    // TMEM: two k-block slots of four group buffers of BN columns. The shared memory request is raised so that no
+    // more CTAs than an SM's 512 columns hold can be resident (an allocation never has to wait).
+    static constexpr int kCols = 8 * BN < 32 ? 32 : 8 * BN;
+    static constexpr size_t kFloor = 233472 / (512 / kCols + 1) + 1024;
+    static constexpr size_t kBytes = kNatural > kFloor ? kNatural : kFloor;
+    static_assert(kCols <= 512 && kBytes <= 232448, "tensor memory or shared memory per CTA");
 };
+
+// Unpacks the packed int4 tile of a stage ([128 rows][64 bytes]) into its int8 operand tile ([128 rows][128 bytes],
+// 16-byte chunk c of row r stored at chunk c ^ (r & 7): the 128-byte swizzle the TMA applies to the int8 tiles).
+// Shared by the nthreads threads of the calling warps (thread index i); ends with the proxy fence that makes the
+// generic-proxy writes visible to the MMA.
+__device__ __forceinline__ void unpack_tile(const uint8_t *raw, uint8_t *a, int i, int nthreads) {
+#pragma unroll 4
+    for (int u = i; u < kBM * 8; u += nthreads) {
+        const int r = u >> 3, c = u & 7;
+        const uint2 pk = *reinterpret_cast<const uint2 *>(raw + r * (kBK / 2) + c * 8);
+        const uint2 e0 = unpack_int4(pk.x), e1 = unpack_int4(pk.y);
+        *reinterpret_cast<uint4 *>(a + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
+            make_uint4(e0.x, e0.y, e1.x, e1.y);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 template <int BN, int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_x, const GemmParams p) {
     using S = Smem<BN, BITS>;
+    constexpr int kLag = 2;  // k-blocks the epilogue warps unpack ahead of the one they finish (int4)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * S::kStage);
-    uint64_t *full = bar, *empty = bar + kStages, *ready = bar + 2 * kStages, *tfull = bar + 3 * kStages,
-             *tempty = tfull + kTmemBufs;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + kTmemBufs);
-    constexpr int kCols = kTmemBufs * BN < 32 ? 32 : kTmemBufs * BN;  // power of two >= 32
+    // full: the stage's copies landed. ready: its int4 tile is unpacked (8 epilogue warps). empty: the epilogue
+    // has finished the stage's k-block (8 warps; its MMAs had completed before that). tfull / tempty: a TMEM
+    // k-block slot was written (one commit) / has been read (8 warps).
+    uint64_t *full = bar, *ready = bar + kStages, *empty = bar + 2 * kStages, *tfull = bar + 3 * kStages,
+             *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    constexpr int kCols = S::kCols;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * kBM, m0 = blockIdx.y * BN;
@@ -194,10 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-            mbar_init(&ready[s], 1);
+            mbar_init(&ready[s], kEpiWarps);
+            mbar_init(&empty[s], kEpiWarps);
         }
-        for (int j = 0; j < kTmemBufs; j++) {
+        for (int j = 0; j < 2; j++) {
             mbar_init(&tfull[j], 1);
             mbar_init(&tempty[j], kEpiWarps);
         }
@@ -217,125 +273,115 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto stage_a = [&](int s) { return smem + (size_t)s * S::kStage; };
     auto stage_b = [&](int s) { return smem + (size_t)s * S::kStage + S::kA; };
     auto stage_raw = [&](int s) { return smem + (size_t)s * S::kStage + S::kA + S::kB; };
-    constexpr uint32_t kTx = (BITS == 4 ? kBM * kBK / 2 : kBM * kBK) + BN * kBK;
+    auto stage_x = [&](int s) { return reinterpret_cast<float *>(smem + (size_t)s * S::kStage + S::kA + S::kB + S::kRaw); };
+    constexpr uint32_t kTx = (BITS == 4 ? kBM * kBK / 2 : kBM * kBK) + BN * kBK + 4 * BN * 4;
 
     if (warp == 0) {
-        // ---------------- producer (and int4 unpacker) ----------------
-        int issued = 0;  // k-blocks whose loads were issued
-        auto issue = [&](int kb) -> bool {
-            const int s = kb % kStages;
-            if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, kErrEmptyWait)) return false;
-            if (lane == 0) {
+        // ---------------- producer: one thread issues the copies of each stage ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, kErrEmptyWait)) break;
                 mbar_expect_tx(&full[s], kTx);
                 if (BITS == 4) tma_load_2d(stage_raw(s), &map_a, &full[s], kb * (kBK / 2), row0);
                 else tma_load_2d(stage_a(s), &map_a, &full[s], kb * kBK, row0);
                 tma_load_2d(stage_b(s), &map_b, &full[s], kb * kBK, m0);
-            }
-            __syncwarp();
-            return true;
-        };
-        bool ok = true;
-        for (int kb = 0; kb < nkb && kb < kStages - 1 && ok; kb++) ok = issue(kb) && ++issued;
-        for (int kb = 0; kb < nkb && ok; kb++) {
-            if (kb + kStages - 1 < nkb) {
-                ok = issue(kb + kStages - 1);
-                if (!ok) break;
+                tma_load_2d(stage_x(s), &map_x, &full[s], m0, kb * (kBK / 32));
                 issued++;
             }
-            if (BITS == 4) {
-                const int s = kb % kStages;
-                if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrRaw)) { ok = false; break; }
-                // packed [128 rows][64 bytes] -> int8 [128 rows][128 bytes], 16-byte chunk c of row r stored at
-                // chunk c ^ (r & 7) (the 128-byte swizzle the TMA applies to the int8 tiles)
-                const uint8_t *raw = stage_raw(s);
-                uint8_t *a = stage_a(s);
-#pragma unroll 4
-                for (int it = 0; it < kBM / 4; it++) {
-                    const int r = it * 4 + (lane >> 3), c = lane & 7;
-                    const uint2 pk = *reinterpret_cast<const uint2 *>(raw + r * (kBK / 2) + c * 8);
-                    const uint2 e0 = unpack_int4(pk.x), e1 = unpack_int4(pk.y);
-                    *reinterpret_cast<uint4 *>(a + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
-                        make_uint4(e0.x, e0.y, e1.x, e1.y);
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ready[s]);
-            }
+            // copies still in flight land before the CTA can end: wait (bounded) for the last phase of each stage
+            for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; kb++)
+                mbar_wait(&full[kb % kStages], (kb / kStages) & 1, kErrFullWait);
         }
-        // copies still in flight land before the CTA can end: wait (bounded) for the last phase of each stage
-        for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; kb++)
-            mbar_wait(&full[kb % kStages], (kb / kStages) & 1, kErrFullWait);
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        const uint32_t idesc = idesc_i8(kBM, BN);
-        bool ok = true;
-        int t = 0;  // group index over the whole K
-        for (int kb = 0; kb < nkb && ok; kb++) {
-            const int s = kb % kStages;
-            if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrFullWait)) break;
-            if (BITS == 4 && !mbar_wait(&ready[s], (kb / kStages) & 1, kErrRaw)) break;
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(stage_a(s)), b0 = smem_u32(stage_b(s));
-            for (int k = 0; k < kBK / 32 && t < ngroups; k++, t++) {
-                const int j = t % kTmemBufs;
-                if (t >= kTmemBufs && !mbar_wait(&tempty[j], ((t / kTmemBufs) - 1) & 1, kErrTmemEmpty)) {
-                    ok = false;
-                    break;
-                }
+        // ---------------- MMA issue: one thread ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_i8(kBM, BN);
+            int kb = 0;
+            for (; kb < nkb; kb++) {
+                const int s = kb % kStages, slot = kb & 1;
+                if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrFullWait)) break;
+                if (BITS == 4 && !mbar_wait(&ready[s], (kb / kStages) & 1, kErrRaw)) break;
+                // the slot's previous k-block must have been read by the epilogue
+                if (kb >= 2 && !mbar_wait(&tempty[slot], ((kb >> 1) - 1) & 1, kErrTmemEmpty)) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    mma_i8(tmem + j * BN, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc);
-                    mma_commit(&tfull[j]);
-                }
-                __syncwarp();
+                const uint32_t a0 = smem_u32(stage_a(s)), b0 = smem_u32(stage_b(s));
+                const int ng_kb = min(kBK / 32, ngroups - kb * (kBK / 32));
+                for (int k = 0; k < ng_kb; k++)
+                    mma_i8(tmem + (slot * 4 + k) * BN, smem_desc(a0 + 32 * k), smem_desc(b0 + 32 * k), idesc);
+                mma_commit(&tfull[slot]);
             }
-            if (lane == 0) mma_commit(&empty[s]);
-            __syncwarp();
+            // all MMAs complete before tensor memory is freed: wait (bounded) for the last commit
+            if (kb > 0) mbar_wait(&tfull[(kb - 1) & 1], ((kb - 1) >> 1) & 1, kErrTmemFull);
         }
-        // all MMAs complete before tensor memory is freed: wait (bounded) for the last commit
-        if (t > 0) mbar_wait(&tfull[(t - 1) % kTmemBufs], ((t - 1) / kTmemBufs) & 1, kErrTmemFull);
     } else {
-        // ---------------- epilogue ----------------
-        constexpr int kCw = BN / 2;  // columns per thread
+        // ---------------- epilogue (and int4 unpack, kLag k-blocks ahead) ----------------
+        constexpr int kCw = BN / 2;               // columns per thread
+        constexpr int kLd = kCw < 32 ? kCw : 32;  // columns per TMEM load
         const int q = warp & 3, half = (warp - 2) >> 2;
         const int row = row0 + q * 32 + lane;
         const int col0 = half * kCw;
+        const int et = threadIdx.x - 64;  // 0 .. 255
         float acc[kCw];
 #pragma unroll
         for (int c = 0; c < kCw; c++) acc[c] = 0.0f;
         const uint16_t *wsr = p.ws + (size_t)(row < p.d ? row : 0) * p.ng;
-        for (int t = 0; t < ngroups; t++) {
-            const int j = t % kTmemBufs;
-            // this row's scale of the group, loaded while the MMA runs
-            const float wsc = scale_from_f16(__ldg(wsr + t));
-            const float ncw = __fmul_rn(-12582912.0f, wsc);  // exact: wsc has <= 11 significant bits
-            const float *xsg = p.xs + (size_t)t * p.ldx + m0 + col0;
-            if (!mbar_wait(&tfull[j], (t / kTmemBufs) & 1, kErrTmemFull)) break;
-            tc_fence_after();
-            int isum[kCw];
+        bool ok = true;
+        auto unpack = [&](int kb) -> bool {  // unpack k-block kb (int4), all 8 warps
+            const int s = kb % kStages;
+            if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrRaw)) return false;
+            unpack_tile(stage_raw(s), stage_a(s), et, 256);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ready[s]);
+            return true;
+        };
+        if (BITS == 4)
+            for (int kb = 0; kb < kLag && kb < nkb && ok; kb++) ok = unpack(kb);
+        uint16_t wnext[4];
 #pragma unroll
-            for (int c = 0; c < kCw; c += 8) {
-                int r8[8];
-                tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + j * BN + col0 + c, r8);
+        for (int k = 0; k < 4; k++) wnext[k] = k < ngroups ? __ldg(wsr + k) : (uint16_t)0;
+        for (int kb = 0; kb < nkb && ok; kb++) {
+            const int s = kb % kStages, slot = kb & 1;
+            if (BITS == 4 && kb + kLag < nkb && !(ok = unpack(kb + kLag))) break;
+            uint16_t wcur[4];
 #pragma unroll
-                for (int i = 0; i < 8; i++) isum[c + i] = r8[i];
+            for (int k = 0; k < 4; k++) {
+                wcur[k] = wnext[k];
+                const int g = (kb + 1) * 4 + k;  // this row's scales of the next k-block, loaded ahead
+                wnext[k] = g < ngroups ? __ldg(wsr + g) : (uint16_t)0;
             }
-            tmem_wait_ld();
+            if (!mbar_wait(&full[s], (kb / kStages) & 1, kErrFullWait)) break;  // the token scales of this stage
+            if (!mbar_wait(&tfull[slot], (kb >> 1) & 1, kErrTmemFull)) break;
+            tc_fence_after();
+            const float *xst = stage_x(s);
+            const int ng_kb = min(kBK / 32, ngroups - kb * (kBK / 32));
+            for (int k = 0; k < ng_kb; k++) {
+                const float wsc = scale_from_f16(wcur[k]);
+                const float ncw = __fmul_rn(-12582912.0f, wsc);  // exact: wsc has <= 11 significant bits
+                int isum[kCw / kLd][kLd];
+#pragma unroll
+                for (int ch = 0; ch < kCw / kLd; ch++)
+                    tmem_ld<kLd>(tmem + ((uint32_t)(q * 32) << 16) + (slot * 4 + k) * BN + col0 + ch * kLd, isum[ch]);
+                tmem_wait_ld();
+                const float *xsg = xst + k * BN + col0;
+#pragma unroll
+                for (int c = 0; c < kCw; c += 4) {
+                    const float4 x4 = *reinterpret_cast<const float4 *>(xsg + c);  // same address in every lane
+                    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float v = __int_as_float(isum[(c + i) / kLd][(c + i) % kLd] + 0x4B400000);
+                        const float pw = __fmaf_rn(v, wsc, ncw);  // fl(isum * ws)
+                        acc[c + i] = __fadd_rn(acc[c + i], __fmul_rn(pw, xv[i]));
+                    }
+                }
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[j]);
-#pragma unroll
-            for (int c = 0; c < kCw; c += 4) {
-                // the tokens' scales of this group (the same address in every lane: one broadcast load)
-                float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (m0 + col0 + c < p.m) x4 = __ldg(reinterpret_cast<const float4 *>(xsg + c));
-                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float v = __int_as_float(isum[c + i] + 0x4B400000);
-                    const float pw = __fmaf_rn(v, wsc, ncw);  // fl(isum * ws)
-                    acc[c + i] = __fadd_rn(acc[c + i], __fmul_rn(pw, xv[i]));
-                }
+            if (lane == 0) {
+                mbar_arrive(&tempty[slot]);
+                mbar_arrive(&empty[s]);
             }
         }
         if (!failed() && row < p.d) {
@@ -367,27 +413,31 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D uint8 tensor map over rows x cols bytes (row pitch cols), box box_rows x box_cols, optional 128B swizzle.
+// 2-D tensor map over rows x cols elements (row pitch cols elements), box box_rows x box_cols, optional 128B
+// swizzle; uint8 or fp32 elements.
 static bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t box_cols,
-                     uint32_t box_rows, bool swizzle) {
+                     uint32_t box_rows, bool swizzle, bool fp32 = false) {
     auto fn = encode_fn();
     if (!fn) return false;
+    const uint64_t esz = fp32 ? 4 : 1;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols};
+    const cuuint64_t strides[1] = {cols * esz};
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int BN, int BITS>
-static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, const GemmParams &p, cudaStream_t s) {
+static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mx, const GemmParams &p,
+                               cudaStream_t s) {
     const size_t smem = Smem<BN, BITS>::kBytes;
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.d + kBM - 1) / kBM, (p.m + BN - 1) / BN);
-    gemm_kernel<BN, BITS><<<grid, kThreads, smem, s>>>(ma, mb, p);
+    gemm_kernel<BN, BITS><<<grid, kThreads, smem, s>>>(ma, mb, mx, p);
     return cudaGetLastError();
 }
 
@@ -426,20 +476,31 @@ extern "C" int mvb_gemm4(const void *w, const void *ws, const void *xq, const fl
     p.m = m;
     p.ldx = ldx;
     p.ng = n / 32;
-    const int bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+    // token tile: the largest of 64, 32, 16 that still gives a CTA per SM (row tiles x token tiles >= 148), or
+    // the smallest that covers m when the matrix is too small to fill the GPU either way
+    const int row_tiles = (d + kBM - 1) / kBM;
+    int bn = 16;
+    for (int c : {64, 32}) {
+        if (c < 2 * m && (long)row_tiles * ((m + c - 1) / c) >= 148) {
+            bn = c;
+            break;
+        }
+    }
     const bool ok_b = make_map(&mb, xq, (uint64_t)n, (uint64_t)m, kBK, bn, true);
-    if (!ok_a || !ok_b) {
+    CUtensorMap mx;  // token scales, group-major: box of 4 groups x bn tokens
+    const bool ok_x = make_map(&mx, xs, (uint64_t)ldx, (uint64_t)(n / 32), bn, kBK / 32, false, true);
+    if (!ok_a || !ok_b || !ok_x) {
         set_error("mvb_gemm4: cannot build the TMA descriptors (driver entry point missing or bad layout)");
         return -1;
     }
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;
     if (wbits == 4) {
-        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, p, s) : bn == 32 ? launch_gemm<32, 4>(ma, mb, p, s)
-          : bn == 64 ? launch_gemm<64, 4>(ma, mb, p, s) : launch_gemm<128, 4>(ma, mb, p, s);
+        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, mx, p, s) : bn == 32 ? launch_gemm<32, 4>(ma, mb, mx, p, s)
+                                                           : launch_gemm<64, 4>(ma, mb, mx, p, s);
     } else {
-        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, p, s) : bn == 32 ? launch_gemm<32, 8>(ma, mb, p, s)
-          : bn == 64 ? launch_gemm<64, 8>(ma, mb, p, s) : launch_gemm<128, 8>(ma, mb, p, s);
+        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, mx, p, s) : bn == 32 ? launch_gemm<32, 8>(ma, mb, mx, p, s)
+                                                           : launch_gemm<64, 8>(ma, mb, mx, p, s);
     }
     if (e != cudaSuccess) {
         set_error("mvb_gemm4: launch failed: %s", cudaGetErrorString(e));
