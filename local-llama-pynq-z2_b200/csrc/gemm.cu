@@ -9,21 +9,24 @@
 // int32 sum for a 128-row x BN-token tile into tensor memory, and the epilogue warps apply the two rounded
 // scale multiplies and the in-order add per group in fp32 registers.
 //
-// CTA = 128 weight rows x BN tokens; K is walked in blocks of 128 bytes (4 groups). Warp roles (320 threads):
+// CTA = 128 weight rows x BN tokens; K is walked in blocks of 128 bytes (4 groups) through a ring of 4
+// shared-memory stages. Warp roles (320 threads):
 //   warp 0   TMA producer (one thread): per k-block the weight tile (int8, or packed int4), the token tile
 //            (both 128-byte swizzled, the layout the MMA descriptors describe) and the tokens' scales of the
-//            block's four groups into a ring of shared-memory stages.
-//   warp 1   allocates tensor memory; for int4 weights its 32 lanes unpack each packed tile into the int8
-//            operand tile (same swizzle); one thread issues the MMAs: per group, D[buffer] = A_g x B_g^T into a
-//            ring of 4 TMEM buffers of BN columns, committed to that buffer's barrier. MMAs run asynchronously,
-//            so the next tile's unpack overlaps them. A stage is free once its MMAs completed (a commit) and
-//            every epilogue warp has read its token scales.
-//   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. Per
-//            group: tcgen05.ld of the int32 sums, release the buffer, then per column
+//            block's four groups ([4][BN] fp32) into the next stage.
+//   warp 1   allocates tensor memory; one thread issues the MMAs: per k-block, D[slot][k] = A_k x B_k^T for its
+//            four groups into one of two TMEM slots of four BN-column group buffers, then one commit. MMAs run
+//            asynchronously, one k-block ahead of the epilogue.
+//   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. For
+//            int4 weights they first unpack the packed tile of the k-block kStages/2 ahead into its int8
+//            operand tile (same swizzle), four 16-byte chunks per thread. Per k-block: tcgen05.ld of the
+//            groups' int32 sums, release the slot and the stage, then per group and column
 //            acc += fl(fl((float)isum * ws) * xs). (float)isum * ws is one fma on a biased integer: with
 //            v = bits(isum + 0x4B400000) = 12582912 + isum (exact for |isum| < 2^22), fma(v, ws, -12582912 * ws)
 //            rounds (v - 12582912) * ws = isum * ws once, and -12582912 * ws is exact because ws has at most 11
 //            significant bits (an fp16 value).
+// The token tile BN (16, 32 or 64) is chosen so that row tiles x token tiles fill the 148 SMs where possible:
+// the in-order sum over groups rules out splitting K across CTAs.
 // Every mbarrier wait is bounded (kGemmWaitNs of %globaltimer); a wait that runs out records an error, the
 // roles stop, outstanding copies and MMAs are waited for (bounded), tensor memory is freed and the kernel ends.
 // No TMA multicast; no clusters.
@@ -43,7 +46,6 @@ namespace gemm {
 
 constexpr int kBM = 128;          // weight rows per CTA (MMA M)
 constexpr int kBK = 128;          // int8 K bytes per stage (4 groups)
-constexpr int kStages = 4;
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr unsigned long long kGemmWaitNs = 1000000000ull;
@@ -200,6 +202,8 @@ struct Smem {
     static constexpr int kRaw = BITS == 4 ? kBM * kBK / 2 : 0;  // packed int4 tile
     static constexpr int kX = 4 * BN * 4;                       // token scales
     static constexpr int kStage = (kA + kB + kRaw + kX + 1023) / 1024 * 1024;
+    // four stages (measured: six to eight, which fit in shared memory, were slower: fewer resident CTAs)
+    static constexpr int kStages = 4;
     static constexpr size_t kNatural = (size_t)kStages * kStage + 1024 /* align */ + 256 /* barriers */;
     // TMEM: two k-block slots of four group buffers of BN columns. The shared memory request is raised so that no
     // more CTAs than an SM's 512 columns hold can be resident (an allocation never has to wait).
@@ -230,7 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_x, const GemmParams p) {
     using S = Smem<BN, BITS>;
-    constexpr int kLag = 2;  // k-blocks the epilogue warps unpack ahead of the one they finish (int4)
+    constexpr int kStages = S::kStages;
+    constexpr int kLag = kStages / 2;  // k-blocks the epilogue warps unpack ahead of the one they finish (int4)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * S::kStage);
@@ -356,24 +361,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float *xst = stage_x(s);
             const int ng_kb = min(kBK / 32, ngroups - kb * (kBK / 32));
-            for (int k = 0; k < ng_kb; k++) {
-                const float wsc = scale_from_f16(wcur[k]);
-                const float ncw = __fmul_rn(-12582912.0f, wsc);  // exact: wsc has <= 11 significant bits
-                int isum[kCw / kLd][kLd];
+            // the block's group sums are read kG groups per TMEM round trip (all four when they fit in registers)
+            constexpr int kG = kCw <= 16 ? 4 : 2;
 #pragma unroll
-                for (int ch = 0; ch < kCw / kLd; ch++)
-                    tmem_ld<kLd>(tmem + ((uint32_t)(q * 32) << 16) + (slot * 4 + k) * BN + col0 + ch * kLd, isum[ch]);
+            for (int k0 = 0; k0 < 4; k0 += kG) {
+                if (k0 >= ng_kb) break;
+                int isum[kG][kCw / kLd][kLd];
+#pragma unroll
+                for (int g = 0; g < kG; g++)
+#pragma unroll
+                    for (int ch = 0; ch < kCw / kLd; ch++)
+                        tmem_ld<kLd>(tmem + ((uint32_t)(q * 32) << 16) + (slot * 4 + k0 + g) * BN + col0 + ch * kLd,
+                                     isum[g][ch]);
                 tmem_wait_ld();
-                const float *xsg = xst + k * BN + col0;
 #pragma unroll
-                for (int c = 0; c < kCw; c += 4) {
-                    const float4 x4 = *reinterpret_cast<const float4 *>(xsg + c);  // same address in every lane
-                    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+                for (int g = 0; g < kG; g++) {
+                    const int k = k0 + g;
+                    if (k >= ng_kb) break;
+                    const float wsc = scale_from_f16(wcur[k]);
+                    const float ncw = __fmul_rn(-12582912.0f, wsc);  // exact: wsc has <= 11 significant bits
+                    const float *xsg = xst + k * BN + col0;
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float v = __int_as_float(isum[(c + i) / kLd][(c + i) % kLd] + 0x4B400000);
-                        const float pw = __fmaf_rn(v, wsc, ncw);  // fl(isum * ws)
-                        acc[c + i] = __fadd_rn(acc[c + i], __fmul_rn(pw, xv[i]));
+                    for (int c = 0; c < kCw; c += 4) {
+                        const float4 x4 = *reinterpret_cast<const float4 *>(xsg + c);  // same address in every lane
+                        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const float v = __int_as_float(isum[g][(c + i) / kLd][(c + i) % kLd] + 0x4B400000);
+                            const float pw = __fmaf_rn(v, wsc, ncw);  // fl(isum * ws)
+                            acc[c + i] = __fadd_rn(acc[c + i], __fmul_rn(pw, xv[i]));
+                        }
                     }
                 }
             }
