@@ -65,8 +65,18 @@ void *mvb_qwen_stream(void *model);
 int mvb_qwen_forward(void *model, int token, int pos, float *logits);
 
 /* Feeds prompt[0 .. n-2] at positions 0 .. n-2 and leaves prompt[n-1] as the input of position n-1, like
- * qwen.c generate() before its first sampled token. 0, or -1. */
+ * qwen.c generate() before its first sampled token. The fed tokens run through the layers in batches of up to 256
+ * with the tensor-core matmul (mvb_gemm4) and a batched causal attention, writing the KV-cache rows one decode
+ * step per token would write, bit for bit (qwen.c computes the logits of prompt positions and discards them;
+ * this skips the head there). 0, or -1. */
 int mvb_qwen_prefill(void *model, const int *prompt, int n);
+
+/* mvb_qwen_prefill's result reached one decode step per fed token (the reference's order of work). 0, or -1. */
+int mvb_qwen_prefill_tokenwise(void *model, const int *prompt, int n);
+
+/* Copies the KV-cache rows of positions 0 .. positions-1 of every layer into k and v (host arrays of n_layers *
+ * positions * kv_dim floats, layer-major). 0, or -1. */
+int mvb_qwen_cache(void *model, int positions, float *k, float *v);
 
 /* Greedy decode of `steps` tokens from the current state; their token ids go to ids (host). Returns steps or -1. */
 int mvb_qwen_decode(void *model, int steps, int *ids);

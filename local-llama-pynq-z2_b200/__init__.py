@@ -70,6 +70,10 @@ def lib():
         L.mvb_qwen_forward.argtypes = [vp, i, i, vp]
         L.mvb_qwen_prefill.restype = i
         L.mvb_qwen_prefill.argtypes = [vp, ip, i]
+        L.mvb_qwen_prefill_tokenwise.restype = i
+        L.mvb_qwen_prefill_tokenwise.argtypes = [vp, ip, i]
+        L.mvb_qwen_cache.restype = i
+        L.mvb_qwen_cache.argtypes = [vp, i, C.POINTER(C.c_float), C.POINTER(C.c_float)]
         L.mvb_qwen_decode.restype = i
         L.mvb_qwen_decode.argtypes = [vp, i, ip]
         L.mvb_qwen_generate.restype = i
@@ -349,6 +353,22 @@ class QwenDecoder:
     def prefill(self, prompt):
         p = self._ids(prompt)
         check(lib().mvb_qwen_prefill(self.h, p.ctypes.data_as(C.POINTER(C.c_int)), p.size), "mvb_qwen_prefill")
+
+    def prefill_tokenwise(self, prompt):
+        """The same state as prefill(), reached one decode step per fed token."""
+        p = self._ids(prompt)
+        check(lib().mvb_qwen_prefill_tokenwise(self.h, p.ctypes.data_as(C.POINTER(C.c_int)), p.size),
+              "mvb_qwen_prefill_tokenwise")
+
+    def cache(self, positions):
+        """(k, v): the KV-cache rows of positions 0 .. positions-1, arrays (n_layers, positions, kv_dim)."""
+        import numpy as np
+        kvd = self.cfg["n_kv_heads"] * (self.cfg["dim"] // self.cfg["n_heads"])
+        k = np.empty((self.cfg["n_layers"], positions, kvd), np.float32)
+        v = np.empty_like(k)
+        f = C.POINTER(C.c_float)
+        check(lib().mvb_qwen_cache(self.h, positions, k.ctypes.data_as(f), v.ctypes.data_as(f)), "mvb_qwen_cache")
+        return k, v
 
     def decode(self, steps):
         import numpy as np

@@ -164,8 +164,8 @@ __device__ __forceinline__ uint2 unpack_int4(uint32_t w) {
 struct GemmParams {
     const uint16_t *ws;  // d x ng fp16 weight scales
     const float *xs;     // ng x ldx fp32 token scales, group-major
-    float *out;          // m x d fp32, token-major
-    int n, d, m, ldx, ng;
+    float *out;          // m rows of ldo fp32 (the first d used), token-major
+    int n, d, m, ldx, ng, ldo;
 };
 
 // N consecutive 32-bit TMEM columns (N = 8, 16 or 32) of this thread's lane.
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!failed() && row < p.d) {
 #pragma unroll
             for (int c = 0; c < kCw; c++)
-                if (m0 + col0 + c < p.m) p.out[(size_t)(m0 + col0 + c) * p.d + row] = acc[c];
+                if (m0 + col0 + c < p.m) p.out[(size_t)(m0 + col0 + c) * p.ldo + row] = acc[c];
         }
     }
     tc_fence_before();
@@ -464,13 +464,15 @@ static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, con
 using namespace mvb;
 using namespace mvb::gemm;
 
-extern "C" int mvb_gemm4(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m,
-                         int ldx, int wbits, void *stream) {
+namespace mvb {
+
+int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m, int ldx,
+                int ldo, int wbits, cudaStream_t stream) {
     if (wbits != 4 && wbits != 8) {
         set_error("mvb_gemm4: unsupported wbits=%d (need 4 or 8)", wbits);
         return -1;
     }
-    if (n <= 0 || n % 32 || n > kMaxN || d <= 0 || m <= 0 || ldx < m || ldx % 4) {
+    if (n <= 0 || n % 32 || n > kMaxN || d <= 0 || m <= 0 || ldx < m || ldx % 4 || ldo < d) {
         set_error("mvb_gemm4: unsupported n=%d d=%d m=%d ldx=%d (need n %% 32 == 0, n <= %d, d, m >= 1, ldx >= m, "
                   "ldx %% 4 == 0)", n, d, m, ldx, kMaxN);
         return -1;
@@ -480,21 +482,12 @@ extern "C" int mvb_gemm4(const void *w, const void *ws, const void *xq, const fl
         set_error("mvb_gemm4: null or misaligned pointer (w and xq 16 bytes, xs 16, ws 2, out 4)");
         return -1;
     }
-    CUtensorMap ma, mb;
+    using namespace gemm;
+    CUtensorMap ma, mb, mx;
     const bool ok_a = wbits == 4 ? make_map(&ma, w, (uint64_t)n / 2, (uint64_t)d, kBK / 2, kBM, false)
                                  : make_map(&ma, w, (uint64_t)n, (uint64_t)d, kBK, kBM, true);
-    // the token tile's box height is the instantiation's BN; chosen below
-    GemmParams p;
-    p.ws = static_cast<const uint16_t *>(ws);
-    p.xs = xs;
-    p.out = out;
-    p.n = n;
-    p.d = d;
-    p.m = m;
-    p.ldx = ldx;
-    p.ng = n / 32;
     // token tile: the largest of 64, 32, 16 that still gives a CTA per SM (row tiles x token tiles >= 148), or
-    // the smallest that covers m when the matrix is too small to fill the GPU either way
+    // the smallest when the matrix is too small to fill the GPU either way
     const int row_tiles = (d + kBM - 1) / kBM;
     int bn = 16;
     for (int c : {64, 32}) {
@@ -504,26 +497,42 @@ extern "C" int mvb_gemm4(const void *w, const void *ws, const void *xq, const fl
         }
     }
     const bool ok_b = make_map(&mb, xq, (uint64_t)n, (uint64_t)m, kBK, bn, true);
-    CUtensorMap mx;  // token scales, group-major: box of 4 groups x bn tokens
+    // token scales, group-major: box of 4 groups x bn tokens
     const bool ok_x = make_map(&mx, xs, (uint64_t)ldx, (uint64_t)(n / 32), bn, kBK / 32, false, true);
     if (!ok_a || !ok_b || !ok_x) {
         set_error("mvb_gemm4: cannot build the TMA descriptors (driver entry point missing or bad layout)");
         return -1;
     }
-    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    GemmParams p;
+    p.ws = static_cast<const uint16_t *>(ws);
+    p.xs = xs;
+    p.out = out;
+    p.n = n;
+    p.d = d;
+    p.m = m;
+    p.ldx = ldx;
+    p.ng = n / 32;
+    p.ldo = ldo;
     cudaError_t e;
     if (wbits == 4) {
-        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, mx, p, s) : bn == 32 ? launch_gemm<32, 4>(ma, mb, mx, p, s)
-                                                           : launch_gemm<64, 4>(ma, mb, mx, p, s);
+        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, mx, p, stream) : bn == 32 ? launch_gemm<32, 4>(ma, mb, mx, p, stream)
+                                                               : launch_gemm<64, 4>(ma, mb, mx, p, stream);
     } else {
-        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, mx, p, s) : bn == 32 ? launch_gemm<32, 8>(ma, mb, mx, p, s)
-                                                           : launch_gemm<64, 8>(ma, mb, mx, p, s);
+        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, mx, p, stream) : bn == 32 ? launch_gemm<32, 8>(ma, mb, mx, p, stream)
+                                                               : launch_gemm<64, 8>(ma, mb, mx, p, stream);
     }
     if (e != cudaSuccess) {
         set_error("mvb_gemm4: launch failed: %s", cudaGetErrorString(e));
         return -1;
     }
     return 0;
+}
+
+}  // namespace mvb
+
+extern "C" int mvb_gemm4(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m,
+                         int ldx, int wbits, void *stream) {
+    return gemm_launch(w, ws, xq, xs, out, n, d, m, ldx, d, wbits, static_cast<cudaStream_t>(stream));
 }
 
 // Synchronizes `stream` and returns (and clears) the device error word of the GEMM kernels: 0, or the code of the

@@ -22,4 +22,8 @@ int row_layout(const void *kernel, int n, int gs, int d, int &rt, size_t &smem);
 int resident_slots(const void *kernel, size_t smem);
 int rows_per_tile(int n, int d);
 
+// The tensor-core prefill matmul of gemm.cu (mvb_gemm4) with an output leading dimension: out[t * ldo + i].
+int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m, int ldx,
+                int ldo, int wbits, cudaStream_t stream);
+
 }  // namespace mvb

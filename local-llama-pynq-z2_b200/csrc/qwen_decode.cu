@@ -34,6 +34,7 @@
 #include "../../include/matvec_b200.h"
 #include "decode_kernels.cuh"
 #include "expf_ref.h"
+#include "prefill_kernels.cuh"
 #include "matvec_kernels.cuh"
 #include "mvb_runtime.h"
 
@@ -133,6 +134,13 @@ struct Model {
     std::vector<cudaEvent_t> prof_ev;
     struct Info { const char *kind; int layer; };
     std::vector<Info> info;  // one per kernel of the step, in launch order
+    // batched prefill buffers (allocated on first use): up to `cap` tokens per batch
+    struct Batch {
+        int cap = 0;
+        float *x = nullptr, *qkv = nullptr, *qb = nullptr, *att = nullptr, *out = nullptr, *h1 = nullptr,
+              *h3 = nullptr, *xs = nullptr;
+        int8_t *xq = nullptr;
+    } pf;
 };
 
 // qwen.c:195-199: every array starts on 64 bytes
@@ -298,7 +306,8 @@ static void destroy(Model *m) {
     for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     if (m->ring) cudaFreeHost(m->ring);
     void *bufs[] = {m->image, m->x, m->xb, m->qkv, m->hb, m->logits, m->kcache, m->vcache, m->rope, m->xq_n,
-                    m->xs_n, m->counters, m->prompt, m->ids, m->st};
+                    m->xs_n, m->counters, m->prompt, m->ids, m->st, m->pf.x, m->pf.qkv, m->pf.qb, m->pf.att,
+                    m->pf.out, m->pf.h1, m->pf.h3, m->pf.xs, m->pf.xq};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -332,6 +341,74 @@ static int wait_stream(Model &m, const char *who, double budget_s) {
             return -1;
         }
     }
+}
+
+constexpr int kBatchCap = 256;  // prompt tokens per batched prefill pass
+
+// Runs prompt tokens tokens[0 .. count-1] (device) at positions p0 .. p0+count-1 through every layer as one batch
+// (no head: qwen.c discards the logits of prompt positions), writing their KV-cache rows exactly as the decode
+// step would. Enqueued on the model's stream; 0, or -1 after set_error().
+static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
+    const Config &c = m.c;
+    const int dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, L = c.n_layers, nmax = dim > hid ? dim : hid;
+    Model::Batch &b = m.pf;
+    cudaError_t e = cudaSuccess;
+    if (!b.cap) {
+        const int cap = m.ctx < kBatchCap ? m.ctx : kBatchCap, ldx = (cap + 3) / 4 * 4;
+        if ((e = cudaMalloc(&b.x, (size_t)cap * dim * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.qkv, (size_t)cap * (dim + 2 * kv) * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.qb, (size_t)cap * dim * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.att, (size_t)cap * dim * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.out, (size_t)cap * dim * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.h1, (size_t)cap * hid * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.h3, (size_t)cap * hid * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.xs, (size_t)(nmax / 32) * ldx * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&b.xq, (size_t)cap * nmax)) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attention_rows_smem_bytes<64>(kMaxCtx))) != cudaSuccess) {
+            set_error("mvb_qwen_prefill: batch buffers: %s", cudaGetErrorString(e));
+            return -1;
+        }
+        b.cap = cap;
+    }
+    if (count < 1 || count > b.cap || p0 < 0 || p0 + count > m.ctx) {
+        set_error("mvb_qwen_prefill: batch of %d tokens at %d outside the buffers", count, p0);
+        return -1;
+    }
+    const cudaStream_t s = m.stream;
+    const int ldx = (count + 3) / 4 * 4, T = kThreads;
+    auto gemm = [&](const Mat &w, int n, int d, float *out, int ldo) {
+        return gemm_launch(w.w, w.s, b.xq, b.xs, out, n, d, count, ldx, ldo, 4, s);
+    };
+    embed_rows_kernel<<<count, T, 0, s>>>((const int8_t *)m.emb.w, m.emb.s, tokens, b.x, dim);
+    for (int l = 0; l < L; l++) {
+        norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, m.attn_norm + (size_t)l * dim, c.rms_eps, dim, b.xq,
+                                                             b.xs, ldx);
+        const int ldq = dim + 2 * kv;
+        if (gemm(m.wq[l], dim, dim, b.qkv, ldq) || gemm(m.wk[l], dim, kv, b.qkv + dim, ldq) ||
+            gemm(m.wv[l], dim, kv, b.qkv + dim + kv, ldq))
+            return -1;
+        rope_cache_rows_kernel<<<count, T, 0, s>>>(b.qkv, ldq, m.bq + (size_t)l * dim, m.bk + (size_t)l * kv,
+                                                   m.bv + (size_t)l * kv, m.rope, m.kcache + (size_t)l * m.ctx * kv,
+                                                   m.vcache + (size_t)l * m.ctx * kv, b.qb, p0, dim, kv, m.hs);
+        attention_rows_kernel<64><<<dim3(count, c.n_heads), T, attention_rows_smem_bytes<64>(m.ctx), s>>>(
+            b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
+            c.n_heads / c.n_kv_heads, m.ctx, m.et);
+        quant_rows_kernel<<<count, T, dim * 4, s>>>(b.att, dim, b.xq, b.xs, ldx);
+        if (gemm(m.wo[l], dim, dim, b.out, dim)) return -1;
+        residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
+        norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, m.ffn_norm + (size_t)l * dim, c.rms_eps, dim, b.xq,
+                                                             b.xs, ldx);
+        if (gemm(m.w1[l], dim, hid, b.h1, hid) || gemm(m.w3[l], dim, hid, b.h3, hid)) return -1;
+        swiglu_quant_rows_kernel<<<count, T, hid * 4, s>>>(b.h1, b.h3, hid, m.et, b.xq, b.xs, ldx);
+        if (gemm(m.w2[l], hid, dim, b.out, dim)) return -1;
+        residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+        set_error("mvb_qwen_prefill: launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
 }
 
 }  // namespace qwen
@@ -453,8 +530,10 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
         (e = cudaMemset(m->kcache, 0, kvbytes)) != cudaSuccess || (e = cudaMemset(m->vcache, 0, kvbytes)) != cudaSuccess ||
         (e = cudaMemset(m->st, 0, sizeof(State))) != cudaSuccess ||
         (e = cudaMemset(m->counters, 0, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
+        // the attribute is per kernel, not per model: set it for the largest context any model may have, so that
+        // loading a model with a smaller context never lowers it under another model's launches
         (e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)attention_smem_bytes<64>(m->ctx))) != cudaSuccess)
+                                  (int)attention_smem_bytes<64>(kMaxCtx))) != cudaSuccess)
         return fail("init");
     if ((e = cudaHostAlloc(&m->ring, sizeof(State) * Model::kRing, cudaHostAllocDefault)) != cudaSuccess)
         return fail("pinned state");
@@ -556,25 +635,64 @@ extern "C" int mvb_qwen_forward(void *model, int token, int pos, float *logits) 
     return s.last_row;
 }
 
-// Feeds prompt[0 .. n-2] (positions 0 .. n-2), leaving prompt[n-1] as the token of position n-1: the state
-// qwen.c's generate() is in just before its first sampled token.
-extern "C" int mvb_qwen_prefill(void *model, const int *prompt, int n) {
-    Model *m = static_cast<Model *>(model);
+static int check_prompt(Model *m, const int *prompt, int n, const char *who) {
     if (!m || !prompt || n < 1 || n >= m->ctx) {
-        set_error("mvb_qwen_prefill: need 1 <= n < ctx");
+        set_error("%s: need 1 <= n < ctx", who);
         return -1;
     }
     for (int i = 0; i < n; i++)
         if (prompt[i] < 0 || prompt[i] >= m->c.vocab_size) {
-            set_error("mvb_qwen_prefill: token id %d out of range", prompt[i]);
+            set_error("%s: token id %d out of range", who, prompt[i]);
             return -1;
         }
     if (cudaMemcpyAsync(m->prompt, prompt, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess) {
-        set_error("mvb_qwen_prefill: prompt upload failed");
+        set_error("%s: prompt upload failed", who);
         return -1;
     }
+    return 0;
+}
+
+// Feeds prompt[0 .. n-2] (positions 0 .. n-2), leaving prompt[n-1] as the token of position n-1: the state
+// qwen.c's generate() is in just before its first sampled token. The fed tokens go through the layers in batches
+// (tensor-core matmuls), writing the same KV-cache rows one decode step per token would.
+extern "C" int mvb_qwen_prefill(void *model, const int *prompt, int n) {
+    Model *m = static_cast<Model *>(model);
+    if (check_prompt(m, prompt, n, "mvb_qwen_prefill")) return -1;
+    for (int p0 = 0; p0 < n - 1; p0 += kBatchCap)
+        if (prefill_batch(*m, m->prompt + p0, p0, (n - 1 - p0) < kBatchCap ? n - 1 - p0 : kBatchCap)) return -1;
+    if (set_state(*m, prompt[n - 1], n - 1, n)) return -1;
+    if (wait_stream(*m, "mvb_qwen_prefill", timeout_s() + 0.01 * n)) return -1;
+    const int st = mvb_gemm_status(m->stream);
+    if (st) {
+        set_error("mvb_qwen_prefill: a matmul wait gave up (code %d)", st);
+        return -1;
+    }
+    return 0;
+}
+
+// The same state reached one decode step per fed token (the reference's own order of work).
+extern "C" int mvb_qwen_prefill_tokenwise(void *model, const int *prompt, int n) {
+    Model *m = static_cast<Model *>(model);
+    if (check_prompt(m, prompt, n, "mvb_qwen_prefill_tokenwise")) return -1;
     if (set_state(*m, prompt[0], 0, n) || mvb_qwen_launch(m, n - 1)) return -1;
-    return wait_stream(*m, "mvb_qwen_prefill", timeout_s() + 0.01 * n);
+    return wait_stream(*m, "mvb_qwen_prefill_tokenwise", timeout_s() + 0.01 * n);
+}
+
+// Copies the KV cache rows of positions 0 .. positions-1 of every layer to k and v (host, n_layers * positions *
+// kv_dim floats each, layer-major). 0, or -1.
+extern "C" int mvb_qwen_cache(void *model, int positions, float *k, float *v) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !k || !v || positions < 1 || positions > m->ctx) return -1;
+    const size_t row = (size_t)positions * m->kv_dim * 4;
+    for (int l = 0; l < m->c.n_layers; l++) {
+        const size_t off = (size_t)l * m->ctx * m->kv_dim;
+        if (cudaMemcpyAsync(k + (size_t)l * positions * m->kv_dim, m->kcache + off, row, cudaMemcpyDeviceToHost,
+                            m->stream) != cudaSuccess ||
+            cudaMemcpyAsync(v + (size_t)l * positions * m->kv_dim, m->vcache + off, row, cudaMemcpyDeviceToHost,
+                            m->stream) != cudaSuccess)
+            return -1;
+    }
+    return wait_stream(*m, "mvb_qwen_cache", timeout_s());
 }
 
 // Greedy decode of `steps` tokens from the current state; ids (host) receives them. Returns the count.

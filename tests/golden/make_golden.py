@@ -18,6 +18,7 @@ import hashlib
 import os
 import subprocess
 import sys
+import tempfile
 
 import numpy as np
 
@@ -112,8 +113,7 @@ def main():
                         **{f"{k}.{f}": v for k, c in cases.items() for f, v in c.items()})
 
     # end to end: a tiny Qwen2-structured .qwb through qwen.c forward (prompt fed token by token, greedy)
-    tmp = os.path.join(ROOT, "_work")
-    os.makedirs(tmp, exist_ok=True)
+    tmp = tempfile.mkdtemp()
     path = os.path.join(tmp, "golden_tiny.qwb")
     qwb.write_synthetic_qwb(path, qwb.QWEN_TINY, seed=11)
     digest = hashlib.sha256(open(path, "rb").read()).hexdigest()

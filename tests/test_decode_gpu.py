@@ -33,11 +33,10 @@ def compare_logits(ours, ref):
     assert np.all(diff <= ATOL + RTOL * np.abs(ref))
 
 
-def test_tiny_decode_vs_golden():
+def test_tiny_decode_vs_golden(tmp_path):
     mvb = load_pkg()
     z = golden("qwen_tiny.npz")
-    path = os.path.join(ROOT, "_work", "decode_tiny.qwb")
-    os.makedirs(os.path.dirname(path), exist_ok=True)
+    path = str(tmp_path / "decode_tiny.qwb")
     mvb.qwb.write_synthetic_qwb(path, mvb.qwb.QWEN_TINY, seed=int(z["seed"]))
     dec = mvb.QwenDecoder(path, ctx=int(z["ctx"]))
     try:
@@ -97,15 +96,51 @@ def test_prefill_decode_equals_generate(qwen05b):
     assert dec.decode(24).tolist() == whole
 
 
-def test_load_rejects_bad_images():
+@pytest.mark.parametrize("n", [1, 2, 37, 129, 300])
+def test_batched_prefill_equals_tokenwise(qwen05b, n):
+    """The batched prefill (tensor-core matmuls, batched attention; batches of 256, so 300 tokens take two) writes
+    the KV-cache rows of one decode step per token bit for bit, and decoding continues identically."""
+    _, dec = qwen05b
+    prompt = [int(t) for t in np.random.default_rng(100 + n).integers(0, 151936, n)]
+    dec.prefill_tokenwise(prompt)
+    k_ref, v_ref = dec.cache(max(n - 1, 1))
+    ids_ref = dec.decode(8).tolist()
+    dec.prefill(prompt)
+    k, v = dec.cache(max(n - 1, 1))
+    if n > 1:
+        assert np.array_equal(k.view(np.uint32), k_ref.view(np.uint32))
+        assert np.array_equal(v.view(np.uint32), v_ref.view(np.uint32))
+    assert dec.decode(8).tolist() == ids_ref
+
+
+def test_tiny_batched_prefill_equals_tokenwise(tmp_path):
+    mvb = load_pkg()
+    path = str(tmp_path / "decode_tiny_batched.qwb")
+    mvb.qwb.write_synthetic_qwb(path, mvb.qwb.QWEN_TINY, seed=11)
+    dec = mvb.QwenDecoder(path, ctx=64)
+    try:
+        prompt = [int(t) for t in np.random.default_rng(4).integers(0, 1000, 40)]
+        dec.prefill_tokenwise(prompt)
+        k_ref, v_ref = dec.cache(39)
+        ids_ref = dec.decode(6).tolist()
+        dec.prefill(prompt)
+        k, v = dec.cache(39)
+        assert np.array_equal(k.view(np.uint32), k_ref.view(np.uint32))
+        assert np.array_equal(v.view(np.uint32), v_ref.view(np.uint32))
+        assert dec.decode(6).tolist() == ids_ref
+    finally:
+        dec.close()
+
+
+def test_load_rejects_bad_images(tmp_path):
     mvb = load_pkg()
     with pytest.raises(mvb.MatvecError):
         mvb.QwenDecoder(b"QWB2" + b"\0" * 300)
-    bad = bytearray(open(os.path.join(ROOT, "_work", "decode_tiny.qwb"), "rb").read()) if os.path.exists(
-        os.path.join(ROOT, "_work", "decode_tiny.qwb")) else None
-    if bad is not None:
-        with pytest.raises(mvb.MatvecError):
-            mvb.QwenDecoder(bytes(bad[:-64]))  # size does not match the header (qwen.c:259-262)
+    path = str(tmp_path / "tiny.qwb")
+    mvb.qwb.write_synthetic_qwb(path, mvb.qwb.QWEN_TINY, seed=11)
+    bad = bytearray(open(path, "rb").read())
+    with pytest.raises(mvb.MatvecError):
+        mvb.QwenDecoder(bytes(bad[:-64]))  # size does not match the header (qwen.c:259-262)
 
 
 def test_qwen05b_blocks_bit_exact_at_pos0(qwen05b):

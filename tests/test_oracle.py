@@ -60,12 +60,11 @@ def test_matvec4_tolerance_rule(restatement):
         assert np.all(err <= 1e-5 * np.abs(terms).sum(1) + 0.0), name
 
 
-def test_synthetic_files_reproduce():
+def test_synthetic_files_reproduce(tmp_path):
     """The seeded generators reproduce the exact files the end-to-end fixtures were made from."""
     import hashlib
     qwb = load_pkg().qwb
-    tmp = os.path.join(ROOT, "_work")
-    os.makedirs(tmp, exist_ok=True)
+    tmp = str(tmp_path)
     z = golden("qwen_tiny.npz")
     p = os.path.join(tmp, "t_tiny.qwb")
     qwb.write_synthetic_qwb(p, qwb.QWEN_TINY, seed=int(z["seed"]))
