@@ -246,14 +246,32 @@ def our_arm(args, rank, world, local_rank):
             parts = line.split()
             if len(parts) == 2 and parts[0] == dom:
                 roofline["traffic"] = float(parts[1])
+    # prompt prefill through the public API (host wall clock, the call returns when the cache is written): the
+    # batched path (tensor-core matmuls) and one decode step per fed token
+    def timed_prefill(fn, reps=3):
+        fn(prompt)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn(prompt)
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+    t_pf = timed_prefill(dec.prefill)
+    t_pf_tok = timed_prefill(dec.prefill_tokenwise)
+    prefill = {"fed_tokens": PROMPT_LEN - 1, "ms": round(t_pf * 1000, 3),
+               "tok_s": round((PROMPT_LEN - 1) / t_pf, 1), "tokenwise_ms": round(t_pf_tok * 1000, 3),
+               "tokenwise_tok_s": round((PROMPT_LEN - 1) / t_pf_tok, 1),
+               "how": "mvb_qwen_prefill (batched: tensor-core matmuls) and mvb_qwen_prefill_tokenwise (one decode "
+                      "step per token); host wall clock of the synchronous call, median of 3"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and os.path.exists(REF_QWEN):
         threads = os.cpu_count()
-        tps, n, _, ref_ids = run_reference_qwen(path, prompt, GEN, threads)
+        tps, n, ref_prompt_s, ref_ids = run_reference_qwen(path, prompt, GEN, threads)
         cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
                "sample": f"qwen.c CPU build (-O3 -fopenmp -ffp-contract=off) on the same .qwb and prompt, one run of "
                          f"{n} greedy tokens, its own generated tok/s",
                "same_ids_as_b200": ref_ids == ids_first.tolist()}
+        prefill["reference_prompt_s"] = ref_prompt_s
     dec.close()
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -266,7 +284,7 @@ def our_arm(args, rank, world, local_rank):
                 "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 32,
                         "d2h_bytes_per_step": 4 * GEN + 32},
-                "gpu_launches": args.steps * GEN * cfg["kernels_per_step"], "clocks": clk}
+                "gpu_launches": args.steps * GEN * cfg["kernels_per_step"], "clocks": clk, "prefill": prefill}
         print(json.dumps(line), flush=True)
 
 
@@ -370,7 +388,7 @@ def prefill_mode(args):
         wb = d * n * bits // 8 + d * (n // 32) * 2
         copies = max(2, min(4096, -(-300 * 2**20 // wb)))
         w, sc = _rand_matrix(torch, n, d, bits, copies, gen)
-        for m in (16, 128, 512):
+        for m in ([args.m] if args.m else (16, 128, 512)):
             xq = torch.randint(-127, 128, (m, n), dtype=torch.int8, device="cuda", generator=gen)
             ldx = (m + 3) // 4 * 4
             xs = torch.rand((n // 32, ldx), device="cuda", generator=gen) * 0.05
@@ -503,7 +521,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", default="", help="sweep: run only this shape, rows x columns (e.g. 131072x8192)")
+    ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
+    ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
     ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill"],
                     help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "
                          "prefill (tensor-core matmul over many tokens)")
