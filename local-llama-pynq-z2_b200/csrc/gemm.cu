@@ -25,7 +25,7 @@
 //            v = bits(isum + 0x4B400000) = 12582912 + isum (exact for |isum| < 2^22), fma(v, ws, -12582912 * ws)
 //            rounds (v - 12582912) * ws = isum * ws once, and -12582912 * ws is exact because ws has at most 11
 //            significant bits (an fp16 value).
-// The token tile BN (16, 32 or 64) is chosen so that row tiles x token tiles fill the 148 SMs where possible:
+// The token tile BN (16, 32 or 64) is the largest that keeps row tiles x token tiles at half the SM count or more:
 // the in-order sum over groups rules out splitting K across CTAs.
 // Every mbarrier wait is bounded (kGemmWaitNs of %globaltimer); a wait that runs out records an error, the
 // roles stop, outstanding copies and MMAs are waited for (bounded), tensor memory is freed and the kernel ends.
@@ -486,12 +486,13 @@ int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, 
     CUtensorMap ma, mb, mx;
     const bool ok_a = wbits == 4 ? make_map(&ma, w, (uint64_t)n / 2, (uint64_t)d, kBK / 2, kBM, false)
                                  : make_map(&ma, w, (uint64_t)n, (uint64_t)d, kBK, kBM, true);
-    // token tile: the largest of 64, 32, 16 that still gives a CTA per SM (row tiles x token tiles >= 148), or
-    // the smallest when the matrix is too small to fill the GPU either way
+    // token tile: the largest of 64, 32, 16 that still gives at least half as many CTAs as SMs, else 16 (measured
+    // on the config-4 shapes at 128 and 512 tokens: larger tiles win while the grid stays that wide, e.g. 4864 x
+    // 896 at 128 tokens in 15.1 us with 64 against 20.2 with 32; narrow matrices want the most CTAs)
     const int row_tiles = (d + kBM - 1) / kBM;
     int bn = 16;
     for (int c : {64, 32}) {
-        if (c < 2 * m && (long)row_tiles * ((m + c - 1) / c) >= 148) {
+        if (c < 2 * m && (long)row_tiles * ((m + c - 1) / c) >= 72) {
             bn = c;
             break;
         }
