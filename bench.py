@@ -426,6 +426,32 @@ def prefill_mode(args):
                       "results": out_lines}))
 
 
+def prompt_mode(args):
+    """Config 3's prompt phase alone: the batched prefill of the 127 fed prompt tokens (mvb_qwen_prefill:
+    tensor-core matmuls, batched attention), K times after W warm-ups, device-timed with CUDA events on the
+    model's stream around each call (the call synchronizes before returning)."""
+    import torch
+    mvb = load_pkg()
+    torch.cuda.set_device(0)
+    dec = mvb.QwenDecoder(model_path(0, 1), ctx=512)
+    stream = torch.cuda.ExternalStream(dec.stream_handle)
+    prompt = prompt_ids()
+    for _ in range(args.warmup):
+        dec.prefill(prompt)
+    ts = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dec.prefill(prompt)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    dec.close()
+    ms = statistics.median(ts)
+    print(json.dumps({"mode": "prompt", "fed_tokens": PROMPT_LEN - 1, "ms": round(ms, 3),
+                      "tok_s": round((PROMPT_LEN - 1) / ms * 1000, 1), "steps": args.steps, "warmup": args.warmup}))
+
+
 def sharded_mode(args, rank, world, local_rank):
     """Config 5: one matrix row-sharded across the ranks (contiguous row blocks), each rank's matvec on its
     shard, and every rank ends the step holding the whole fp32 output. Two ways are timed per step with CUDA
@@ -523,9 +549,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
-    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill", "prompt"],
                     help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "
-                         "prefill (tensor-core matmul over many tokens)")
+                         "prefill (tensor-core matmul over many tokens), prompt (batched prompt prefill)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -538,6 +564,9 @@ def main():
         return
     if args.mode == "prefill":
         prefill_mode(args)
+        return
+    if args.mode == "prompt":
+        prompt_mode(args)
         return
     if world > 1:
         import datetime

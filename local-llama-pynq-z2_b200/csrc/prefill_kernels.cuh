@@ -92,20 +92,21 @@ __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const float *src, 
     quantize_row(sm, n, xq + (size_t)t * n, xs + t, ldx);
 }
 
-// SwiGLU of rows t of h1 (gate) and h3 (up) (qwen.c:558-562, the kEpiSwiGLU epilogue), then quantize (the down
-// projection's kProQuant prologue). Dynamic shared memory: n floats.
+// SwiGLU of rows t = blockIdx.x of h1 (gate) and h3 (up) (qwen.c:558-562, the kEpiSwiGLU epilogue), then quantize
+// (the down projection's kProQuant prologue), for the groups [32 * blockIdx.y, 32 * blockIdx.y + 32) of the row:
+// groups are independent, so a token's row is spread over several CTAs. Static shared memory: 32 groups.
 __global__ void __launch_bounds__(kThreads) swiglu_quant_rows_kernel(const float *h1, const float *h3, int n,
                                                                      ExpTable et, int8_t *xq, float *xs, int ldx) {
-    extern __shared__ __align__(16) float sm[];
-    const int t = blockIdx.x;
-    for (int j = threadIdx.x; j < n; j += kThreads) {
-        float gv = __ldcg(h1 + (size_t)t * n + j);
-        const float u = __ldcg(h3 + (size_t)t * n + j);
+    __shared__ __align__(16) float sm[32 * 32];
+    const int t = blockIdx.x, g0 = blockIdx.y * 32, ng = min(32, n / 32 - g0), e0 = g0 * 32;
+    for (int j = threadIdx.x; j < ng * 32; j += kThreads) {
+        float gv = __ldcg(h1 + (size_t)t * n + e0 + j);
+        const float u = __ldcg(h3 + (size_t)t * n + e0 + j);
         gv = __fmul_rn(gv, __frcp_rn(__fadd_rn(1.0f, expf_ref(-gv, et))));  // 1.0f / (...) of qwen.c
         sm[j] = __fmul_rn(gv, u);
     }
     __syncthreads();
-    quantize_row(sm, n, xq + (size_t)t * n, xs + t, ldx);
+    quantize_row(sm, ng * 32, xq + (size_t)t * n + e0, xs + (size_t)g0 * ldx + t, ldx);
 }
 
 // x += add, element by element (the kEpiResidual epilogue: x = x + matvec).
@@ -156,11 +157,12 @@ __global__ void rope_cache_rows_kernel(const float *qkv, int ldq, const float *b
 template <int HS>
 __global__ void __launch_bounds__(kThreads) attention_rows_kernel(const float *qb, const float *kcache,
                                                                   const float *vcache, float *out, int p0, int dim,
-                                                                  int kv_dim, int kv_mul, int ctx, ExpTable et) {
+                                                                  int kv_dim, int kv_mul, int npos, int vchunk,
+                                                                  ExpTable et) {
     extern __shared__ __align__(16) float asm_[];
     float *q = asm_;
-    float *att = q + HS;                    // ctx scores
-    float *vbuf = att + ((ctx + 3) & ~3);   // kVChunk x HS staged values
+    float *att = q + HS;                    // scores of positions 0 .. npos-1 (npos = the batch's last position + 1)
+    float *vbuf = att + ((npos + 3) & ~3);  // vchunk x HS staged values
     __shared__ float red[kThreads / 32];
     __shared__ float s_max, s_sum;
     const int t = blockIdx.x, h = blockIdx.y, kvh = h / kv_mul, tid = threadIdx.x, pos = p0 + t;
@@ -204,8 +206,8 @@ __global__ void __launch_bounds__(kThreads) attention_rows_kernel(const float *q
     for (int u = tid; u <= pos; u += kThreads) att[u] = __fdiv_rn(att[u], sum);
     // weighted values of the cached positions 0 .. pos-1 in order, then this position's
     float acc = 0.0f;
-    for (int t0 = 0; t0 < pos; t0 += kVChunk) {
-        const int nt = min(kVChunk, pos - t0);
+    for (int t0 = 0; t0 < pos; t0 += vchunk) {
+        const int nt = min(vchunk, pos - t0);
         __syncthreads();  // the previous chunk has been read
         stage_values<HS>(vbuf, vcache, kv_dim, kvh, t0, nt);
         cp_async_commit();
@@ -219,9 +221,10 @@ __global__ void __launch_bounds__(kThreads) attention_rows_kernel(const float *q
     }
 }
 
+// Shared memory of attention_rows_kernel for positions 0 .. npos-1 and value chunks of vchunk positions.
 template <int HS>
-inline size_t attention_rows_smem_bytes(int ctx) {
-    return (size_t)HS * 4 + (size_t)((ctx + 3) & ~3) * 4 + (size_t)kVChunk * HS * 4;
+inline size_t attention_rows_smem_bytes(int npos, int vchunk) {
+    return (size_t)HS * 4 + (size_t)((npos + 3) & ~3) * 4 + (size_t)vchunk * HS * 4;
 }
 
 }  // namespace qwen

@@ -365,7 +365,7 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
             (e = cudaMalloc(&b.xs, (size_t)(nmax / 32) * ldx * 4)) != cudaSuccess ||
             (e = cudaMalloc(&b.xq, (size_t)cap * nmax)) != cudaSuccess ||
             (e = cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attention_rows_smem_bytes<64>(kMaxCtx))) != cudaSuccess) {
+                                      (int)attention_rows_smem_bytes<64>(kMaxCtx, kVChunk))) != cudaSuccess) {
             set_error("mvb_qwen_prefill: batch buffers: %s", cudaGetErrorString(e));
             return -1;
         }
@@ -391,16 +391,19 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
         rope_cache_rows_kernel<<<count, T, 0, s>>>(b.qkv, ldq, m.bq + (size_t)l * dim, m.bk + (size_t)l * kv,
                                                    m.bv + (size_t)l * kv, m.rope, m.kcache + (size_t)l * m.ctx * kv,
                                                    m.vcache + (size_t)l * m.ctx * kv, b.qb, p0, dim, kv, m.hs);
-        attention_rows_kernel<64><<<dim3(count, c.n_heads), T, attention_rows_smem_bytes<64>(m.ctx), s>>>(
+        // shared memory for the positions this batch reaches only: more CTAs per SM
+        const int npos = p0 + count, vchunk = npos < kVChunk ? (npos + 7) / 8 * 8 : kVChunk;
+        attention_rows_kernel<64><<<dim3(count, c.n_heads), T, attention_rows_smem_bytes<64>(npos, vchunk), s>>>(
             b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
-            c.n_heads / c.n_kv_heads, m.ctx, m.et);
+            c.n_heads / c.n_kv_heads, npos, vchunk, m.et);
         quant_rows_kernel<<<count, T, dim * 4, s>>>(b.att, dim, b.xq, b.xs, ldx);
         if (gemm(m.wo[l], dim, dim, b.out, dim)) return -1;
         residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
         norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, m.ffn_norm + (size_t)l * dim, c.rms_eps, dim, b.xq,
                                                              b.xs, ldx);
         if (gemm(m.w1[l], dim, hid, b.h1, hid) || gemm(m.w3[l], dim, hid, b.h3, hid)) return -1;
-        swiglu_quant_rows_kernel<<<count, T, hid * 4, s>>>(b.h1, b.h3, hid, m.et, b.xq, b.xs, ldx);
+        swiglu_quant_rows_kernel<<<dim3(count, (hid / 32 + 31) / 32), T, 0, s>>>(b.h1, b.h3, hid, m.et, b.xq, b.xs,
+                                                                                 ldx);
         if (gemm(m.w2[l], hid, dim, b.out, dim)) return -1;
         residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
     }
