@@ -532,12 +532,50 @@ def sharded_mode(args, rank, world, local_rank):
                         "frac_of_aggregate_hbm": round(total / t_fused / 1e9 / (peak * world), 4),
                         "nccl_us_per_step": round(t_step * 1e6, 2), "nccl_allgather_us": round(t_ag * 1e6, 2),
                         "gathered_ok": bool(okt.item())})
+        # batch 32: the tensor-core matmul on each rank's shard; rows gathered by its epilogue (fused) or by an
+        # NCCL all-gather of each rank's [32 x rows] block after a plain matmul
+        m = 32
+        xq32 = torch.randint(-127, 128, (m, n), dtype=torch.int8, device="cuda",
+                             generator=torch.Generator(device="cuda").manual_seed(8))
+        xs32 = torch.full((n // 32, m), 0.01, device="cuda")
+        gb = mvb.ShardGather(rank, world, rows, tokens=m)
+        handles = [None] * world
+        dist.all_gather_object(handles, gb.handle())
+        gb.connect(handles)
+        blk = torch.empty((m, rows), device="cuda")
+        blocks = torch.empty((world, m, rows), device="cuda")
+
+        def fused32(i):
+            gb.gemm4(w[i % copies], sc[i % copies], xq32, xs32, n, m, m, bits)
+
+        def nccl32(i):
+            mvb.gemm4(w[i % copies], sc[i % copies], xq32, xs32, blk, n, rows, m, m, bits)
+            dist.all_gather_into_tensor(blocks, blk)
+
+        t_f32 = timed(fused32, args.steps)
+        t_n32 = timed(nccl32, args.steps)
+        fused32(0)
+        nccl32(0)
+        torch.cuda.synchronize()
+        ok32 = torch.equal(gb.output(), blocks.permute(1, 0, 2).reshape(m, world * rows)) and gb.error() == 0
+        okt = torch.tensor([1 if ok32 else 0], device="cuda")
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+        torch.cuda.synchronize()
+        dist.barrier()
+        gb.close()
+        dist.barrier()
+        results.append({"shape": f"{d}x{n} Q{bits}", "batch": m, "n_gpus": world, "rows_per_gpu": rows,
+                        "us_per_step": round(t_f32 * 1e6, 2), "GBps_total": round(total / t_f32 / 1e9, 1),
+                        "frac_of_aggregate_hbm": round(total / t_f32 / 1e9 / (peak * world), 4),
+                        "tokens_per_s": round(m / t_f32, 1), "nccl_us_per_step": round(t_n32 * 1e6, 2),
+                        "gathered_ok": bool(okt.item())})
         del w, sc
         torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps({"mode": "sharded", "peak_per_gpu": peak, "peak_source": f"{peak_kind} hbm_gbs",
-                          "collective": "fused peer stores (mvb_gather_matvec4); NCCL all_gather_into_tensor "
-                                        "for comparison", "results": results}), flush=True)
+                          "collective": "fused peer stores (mvb_gather_matvec4 at batch 1, mvb_gather_gemm4 at "
+                                        "batch 32); NCCL all_gather_into_tensor for comparison",
+                          "results": results}), flush=True)
 
 
 def main():

@@ -156,6 +156,8 @@ int mvb_gemm_status(void *stream);
  * rank order. Every rank must then make the same sequence of mvb_gather_matvec4 calls with the same n. */
 int mvb_gather_handle_size(void);
 void *mvb_gather_create(int rank, int world, int rows, void *handle);  /* NULL on error */
+/* The same with room for `tokens` tokens per call (mvb_gather_gemm4); mvb_gather_create holds one. */
+void *mvb_gather_create_batch(int rank, int world, int rows, int tokens, void *handle);
 int mvb_gather_connect(void *gather, const void *handles);            /* 0, or -1 */
 
 /* This rank's shard (rows x n, wbits 4 or 8, .qwb layout; xq/xs the full activation vector) on `stream`. The
@@ -164,6 +166,12 @@ int mvb_gather_connect(void *gather, const void *handles);            /* 0, or -
 int mvb_gather_matvec4(void *gather, const void *w, const void *ws, const void *xq, const void *xs, int n, int wbits,
                        void *stream);
 float *mvb_gather_output(void *gather);  /* device pointer of the last call's gathered output */
+
+/* The batched form: m <= tokens tokens (xq m x n int8 token-major, xs n/32 x ldx fp32 group-major, as in
+ * mvb_gemm4) through this rank's shard on the tensor cores; the gathered output is token-major, m x (rows * world)
+ * fp32 (token t's row i of rank r at t * rows * world + r * rows + i). 0, or -1. */
+int mvb_gather_gemm4(void *gather, const void *w, const void *ws, const void *xq, const float *xs, int n, int m,
+                     int ldx, int wbits, void *stream);
 
 /* 1 if a wait gave up (some rank's rows never arrived within 2 s), 0 if none did, -1 on error; synchronizes
  * `stream`. After a 1 the gather's counters no longer match: destroy it and create a new one on every rank. */

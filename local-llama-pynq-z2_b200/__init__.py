@@ -101,6 +101,10 @@ def lib():
         L.mvb_gather_handle_size.restype = i
         L.mvb_gather_create.restype = vp
         L.mvb_gather_create.argtypes = [i, i, i, vp]
+        L.mvb_gather_create_batch.restype = vp
+        L.mvb_gather_create_batch.argtypes = [i, i, i, i, vp]
+        L.mvb_gather_gemm4.restype = i
+        L.mvb_gather_gemm4.argtypes = [vp] * 5 + [i] * 4 + [vp]
         L.mvb_gather_connect.restype = i
         L.mvb_gather_connect.argtypes = [vp, vp]
         L.mvb_gather_matvec4.restype = i
@@ -270,11 +274,12 @@ class ShardGather:
         full = g.output()                        # torch view, rows * world fp32, valid in stream order
     """
 
-    def __init__(self, rank, world, rows):
+    def __init__(self, rank, world, rows, tokens=1):
         L = lib()
-        self.rank, self.world, self.rows = rank, world, rows
+        self.rank, self.world, self.rows, self.tokens = rank, world, rows, tokens
+        self._m = 1
         buf = (C.c_uint8 * L.mvb_gather_handle_size())()
-        self._g = L.mvb_gather_create(rank, world, rows, buf)
+        self._g = L.mvb_gather_create_batch(rank, world, rows, tokens, buf)
         if not self._g:
             raise MatvecError(f"mvb_gather_create failed: {last_error()}")
         self._handle = bytes(buf)
@@ -289,15 +294,24 @@ class ShardGather:
         check(lib().mvb_gather_connect(self._g, C.c_char_p(blob)), "mvb_gather_connect")
 
     def matvec4(self, w, ws, xq, xs, n, wbits, stream=None):
+        self._m = 1
         return check(lib().mvb_gather_matvec4(self._g, _ptr(w), _ptr(ws), _ptr(xq), _ptr(xs), n, wbits,
                                               _stream(stream)), "mvb_gather_matvec4")
+
+    def gemm4(self, w, ws, xq, xs, n, m, ldx, wbits, stream=None):
+        """m tokens (xq (m, n) int8, xs (n/32, ldx) fp32 group-major) through this rank's shard on the tensor cores;
+        output() is then (m, rows * world), token-major."""
+        self._m = m
+        return check(lib().mvb_gather_gemm4(self._g, _ptr(w), _ptr(ws), _ptr(xq), _ptr(xs), n, m, ldx, wbits,
+                                            _stream(stream)), "mvb_gather_gemm4")
 
     def output(self):
         import torch
         ptr = lib().mvb_gather_output(self._g)
         if not ptr:
             raise MatvecError("no gathered output yet (call matvec4 first)")
-        return torch.as_tensor(_DeviceVector(ptr, self.rows * self.world), device="cuda")
+        t = torch.as_tensor(_DeviceVector(ptr, self._m * self.rows * self.world), device="cuda")
+        return t if self._m == 1 else t.view(self._m, self.rows * self.world)
 
     def error(self, stream=None):
         return lib().mvb_gather_error(self._g, _stream(stream))

@@ -33,7 +33,7 @@
 
 namespace mvb {
 
-constexpr int kMaxRanks = 8;
+constexpr int kMaxRanks = kMaxGatherRanks;
 constexpr long kGatherSpin = 1L << 26;
 constexpr unsigned long long kGatherWaitNs = 2000000000ull;
 // Head of each rank's buffer, before the two output buffers: [0] arrival counter, [1] error word, [2] CTA counter.
@@ -110,14 +110,14 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) gather_
 }
 
 struct Gather {
-    int rank = 0, world = 0, rows = 0;
-    uint8_t *mem = nullptr;        // [kGatherHead | output 0 | output 1], each output rows * world fp32
+    int rank = 0, world = 0, rows = 0, tokens = 1;
+    uint8_t *mem = nullptr;        // [kGatherHead | output 0 | output 1], each output tokens x rows * world fp32
     std::vector<uint8_t *> peer;   // every rank's `mem`, mapped here (own included)
     unsigned expected = 0;         // this rank's arrival counter at the end of the last call
     unsigned calls = 0;
 };
 
-static size_t out_bytes(const Gather *g) { return (size_t)g->rows * g->world * 4; }
+static size_t out_bytes(const Gather *g) { return (size_t)g->tokens * g->rows * g->world * 4; }
 
 }  // namespace mvb
 
@@ -125,16 +125,17 @@ using namespace mvb;
 
 extern "C" int mvb_gather_handle_size(void) { return (int)sizeof(cudaIpcMemHandle_t); }
 
-extern "C" void *mvb_gather_create(int rank, int world, int rows, void *handle) {
-    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || rows < 1 || !handle) {
-        set_error("mvb_gather_create: need 1 <= world <= %d, 0 <= rank < world, rows >= 1, a handle buffer",
-                  kMaxRanks);
+extern "C" void *mvb_gather_create_batch(int rank, int world, int rows, int tokens, void *handle) {
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || rows < 1 || tokens < 1 || !handle) {
+        set_error("mvb_gather_create: need 1 <= world <= %d, 0 <= rank < world, rows >= 1, tokens >= 1, a handle "
+                  "buffer", kMaxRanks);
         return nullptr;
     }
     Gather *g = new Gather;
     g->rank = rank;
     g->world = world;
     g->rows = rows;
+    g->tokens = tokens;
     const size_t bytes = kGatherHead + 2 * out_bytes(g);
     cudaError_t e = cudaMalloc(&g->mem, bytes);
     if (e == cudaSuccess) e = cudaMemset(g->mem, 0, bytes);
@@ -149,6 +150,10 @@ extern "C" void *mvb_gather_create(int rank, int world, int rows, void *handle) 
     g->peer.assign(world, nullptr);
     g->peer[rank] = g->mem;
     return g;
+}
+
+extern "C" void *mvb_gather_create(int rank, int world, int rows, void *handle) {
+    return mvb_gather_create_batch(rank, world, rows, 1, handle);
 }
 
 extern "C" int mvb_gather_connect(void *gather, const void *handles) {
@@ -226,6 +231,46 @@ extern "C" int mvb_gather_matvec4(void *gather, const void *w, const void *ws, c
         return -1;
     }
     g->expected = gp.target;
+    g->calls++;
+    return 0;
+}
+
+// The batched form: m tokens through this rank's rows on the tensor cores (gemm.cu), every row stored into
+// every rank's token-major gathered output (m x rows * world fp32) by the matmul's epilogue, completion signalled
+// the same way.
+extern "C" int mvb_gather_gemm4(void *gather, const void *w, const void *ws, const void *xq, const float *xs, int n,
+                                int m, int ldx, int wbits, void *stream) {
+    Gather *g = static_cast<Gather *>(gather);
+    if (!g) {
+        set_error("mvb_gather_gemm4: null gather");
+        return -1;
+    }
+    for (int q = 0; q < g->world; q++)
+        if (!g->peer[q]) {
+            set_error("mvb_gather_gemm4: rank %d's buffer is not mapped (call mvb_gather_connect)", q);
+            return -1;
+        }
+    if (m < 1 || m > g->tokens) {
+        set_error("mvb_gather_gemm4: %d tokens, the gather holds at most %d", m, g->tokens);
+        return -1;
+    }
+    PeerTargets pt = {};
+    const size_t off = kGatherHead + (g->calls & 1) * out_bytes(g);
+    for (int q = 0; q < g->world; q++) {
+        pt.out[q] = reinterpret_cast<float *>(g->peer[q] + off);
+        pt.arrive[q] = reinterpret_cast<unsigned *>(g->peer[q]);
+    }
+    unsigned *head = reinterpret_cast<unsigned *>(g->mem);
+    pt.err = reinterpret_cast<int *>(head + 1);
+    pt.done = head + 2;
+    pt.world = g->world;
+    pt.rank = g->rank;
+    pt.col0 = g->rank * g->rows;
+    pt.target = g->expected + (unsigned)g->world;
+    if (gemm_launch(w, ws, xq, xs, nullptr, n, g->rows, m, ldx, g->rows * g->world, wbits,
+                    static_cast<cudaStream_t>(stream), &pt))
+        return -1;
+    g->expected = pt.target;
     g->calls++;
     return 0;
 }

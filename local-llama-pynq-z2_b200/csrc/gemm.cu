@@ -166,7 +166,11 @@ struct GemmParams {
     const float *xs;     // ng x ldx fp32 token scales, group-major
     float *out;          // m rows of ldo fp32 (the first d used), token-major
     int n, d, m, ldx, ng, ldo;
+    PeerTargets peers;   // GATHER: the gathered outputs and the completion counters
 };
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // N consecutive 32-bit TMEM columns (N = 8, 16 or 32) of this thread's lane.
 template <int N>
@@ -229,7 +233,7 @@ __device__ __forceinline__ void unpack_tile(const uint8_t *raw, uint8_t *a, int 
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int BN, int BITS>
+template <int BN, int BITS, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_x, const GemmParams p) {
@@ -402,16 +406,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (!failed() && row < p.d) {
+            if (!GATHER) {
 #pragma unroll
-            for (int c = 0; c < kCw; c++)
-                if (m0 + col0 + c < p.m) p.out[(size_t)(m0 + col0 + c) * p.ldo + row] = acc[c];
+                for (int c = 0; c < kCw; c++)
+                    if (m0 + col0 + c < p.m) p.out[(size_t)(m0 + col0 + c) * p.ldo + row] = acc[c];
+            } else {
+                // every rank's gathered output: 32 lanes store 32 consecutive rows of one token (NVLink for peers)
+#pragma unroll
+                for (int c = 0; c < kCw; c++)
+                    if (m0 + col0 + c < p.m) {
+                        const size_t o = (size_t)(m0 + col0 + c) * p.ldo + p.peers.col0 + row;
+#pragma unroll
+                        for (int r = 0; r < kMaxGatherRanks; r++)
+                            if (r < p.peers.world) p.peers.out[r][o] = acc[c];
+                    }
+            }
         }
+        if (GATHER) fence_acq_rel_gpu();  // this thread's stores, before the CTA is counted
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    if (GATHER && threadIdx.x == 0 &&
+        atomicAdd(p.peers.done, 1u) == gridDim.x * gridDim.y - 1) {
+        // the last CTA of this rank: every CTA's rows are stored. Signal every rank (one system-scope fence, then
+        // relaxed adds: a release), then wait, bounded, until every rank has signalled this call.
+        *p.peers.done = 0;
+        fence_acq_rel_sys();
+        for (int r = 0; r < kMaxGatherRanks; r++)
+            if (r < p.peers.world)
+                asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(p.peers.arrive[r]) : "memory");
+        const unsigned long long t0 = now_ns();
+        for (uint32_t i = 0;; i++) {
+            unsigned v;
+            asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.peers.arrive[p.peers.rank]) : "memory");
+            if ((int)(v - p.peers.target) >= 0) {
+                fence_acq_rel_sys();
+                break;
+            }
+            if ((i & 63) == 63 && now_ns() - t0 > 2 * kGemmWaitNs) {
+                atomicExch(p.peers.err, 1);
+                break;
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -449,12 +489,13 @@ static bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t
 
 template <int BN, int BITS>
 static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mx, const GemmParams &p,
-                               cudaStream_t s) {
+                               cudaStream_t s, bool gather) {
     const size_t smem = Smem<BN, BITS>::kBytes;
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kernel = gather ? gemm_kernel<BN, BITS, true> : gemm_kernel<BN, BITS, false>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.d + kBM - 1) / kBM, (p.m + BN - 1) / BN);
-    gemm_kernel<BN, BITS><<<grid, kThreads, smem, s>>>(ma, mb, mx, p);
+    kernel<<<grid, kThreads, smem, s>>>(ma, mb, mx, p);
     return cudaGetLastError();
 }
 
@@ -467,7 +508,7 @@ using namespace mvb::gemm;
 namespace mvb {
 
 int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m, int ldx,
-                int ldo, int wbits, cudaStream_t stream) {
+                int ldo, int wbits, cudaStream_t stream, const PeerTargets *peers) {
     if (wbits != 4 && wbits != 8) {
         set_error("mvb_gemm4: unsupported wbits=%d (need 4 or 8)", wbits);
         return -1;
@@ -477,7 +518,7 @@ int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, 
                   "ldx %% 4 == 0)", n, d, m, ldx, kMaxN);
         return -1;
     }
-    if (!w || !ws || !xq || !xs || !out || ((uintptr_t)w & 15) || ((uintptr_t)xq & 15) || ((uintptr_t)ws & 1) ||
+    if (!w || !ws || !xq || !xs || (!out && !peers) || ((uintptr_t)w & 15) || ((uintptr_t)xq & 15) || ((uintptr_t)ws & 1) ||
         ((uintptr_t)xs & 15) || ((uintptr_t)out & 3)) {
         set_error("mvb_gemm4: null or misaligned pointer (w and xq 16 bytes, xs 16, ws 2, out 4)");
         return -1;
@@ -514,13 +555,15 @@ int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, 
     p.ldx = ldx;
     p.ng = n / 32;
     p.ldo = ldo;
+    p.peers = peers ? *peers : PeerTargets{};
+    const bool g = peers != nullptr;
     cudaError_t e;
     if (wbits == 4) {
-        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, mx, p, stream) : bn == 32 ? launch_gemm<32, 4>(ma, mb, mx, p, stream)
-                                                               : launch_gemm<64, 4>(ma, mb, mx, p, stream);
+        e = bn == 16 ? launch_gemm<16, 4>(ma, mb, mx, p, stream, g)
+          : bn == 32 ? launch_gemm<32, 4>(ma, mb, mx, p, stream, g) : launch_gemm<64, 4>(ma, mb, mx, p, stream, g);
     } else {
-        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, mx, p, stream) : bn == 32 ? launch_gemm<32, 8>(ma, mb, mx, p, stream)
-                                                               : launch_gemm<64, 8>(ma, mb, mx, p, stream);
+        e = bn == 16 ? launch_gemm<16, 8>(ma, mb, mx, p, stream, g)
+          : bn == 32 ? launch_gemm<32, 8>(ma, mb, mx, p, stream, g) : launch_gemm<64, 8>(ma, mb, mx, p, stream, g);
     }
     if (e != cudaSuccess) {
         set_error("mvb_gemm4: launch failed: %s", cudaGetErrorString(e));

@@ -22,8 +22,24 @@ int row_layout(const void *kernel, int n, int gs, int d, int &rt, size_t &smem);
 int resident_slots(const void *kernel, size_t smem);
 int rows_per_tile(int n, int d);
 
-// The tensor-core prefill matmul of gemm.cu (mvb_gemm4) with an output leading dimension: out[t * ldo + i].
+// Where a row-sharded matmul stores its rows and how it signals completion (gather.cu's protocol): every rank's
+// gathered output (token-major, ldo floats per token, this rank's rows at columns col0 ..), every rank's arrival
+// counter, this rank's CTA counter and error word, and the value this rank's arrival counter reaches once every
+// rank has signalled this call.
+constexpr int kMaxGatherRanks = 8;
+struct PeerTargets {
+    float *out[kMaxGatherRanks];
+    unsigned *arrive[kMaxGatherRanks];
+    unsigned *done;
+    int *err;
+    int world, rank, col0;
+    unsigned target;
+};
+
+// The tensor-core prefill matmul of gemm.cu (mvb_gemm4) with an output leading dimension: out[t * ldo + i]. With
+// peers, the rows go to every rank's gathered output instead and the call signals completion (the all-gather of a
+// row-sharded matmul fused into it); out is then unused.
 int gemm_launch(const void *w, const void *ws, const void *xq, const float *xs, float *out, int n, int d, int m, int ldx,
-                int ldo, int wbits, cudaStream_t stream);
+                int ldo, int wbits, cudaStream_t stream, const PeerTargets *peers = nullptr);
 
 }  // namespace mvb

@@ -64,6 +64,39 @@ def test_gather_one_rank(mvb, restatement, n, d, bits):
         g.close()
 
 
+def _xs_group_major(xs, m):
+    ldx = (m + 3) // 4 * 4
+    out = np.zeros((xs.shape[1], ldx), np.float32)
+    out[:, :m] = xs.T
+    return out, ldx
+
+
+@pytest.mark.parametrize("n,d,m,bits", [(896, 4864, 32, 4), (8192, 1027, 20, 4), (896, 2048, 32, 8)])
+def test_gather_gemm_one_rank(mvb, restatement, n, d, m, bits):
+    """The batched gather (tensor-core matmul whose epilogue stores into the gathered output): token-major output,
+    every token's row bit-identical to its matvec, over repeated calls."""
+    import torch
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(n + d + m + bits)
+    w, ws = _random_q(rng, n, d, bits)
+    g = mvb.ShardGather(0, 1, d, tokens=m)
+    try:
+        g.connect([g.handle()])
+        wd = torch.from_numpy(w).cuda()
+        wsd = torch.from_numpy(ws.view(np.int16)).cuda()
+        for call in range(3):
+            xq = rng.integers(-128, 128, (m, n)).astype(np.int8)
+            xs = rng.uniform(1e-3, 1e-1, (m, n // 32)).astype(np.float32)
+            xs_gm, ldx = _xs_group_major(xs, m)
+            g.gemm4(wd, wsd, torch.from_numpy(xq).cuda(), torch.from_numpy(xs_gm).cuda(), n, m, ldx, bits)
+            out = g.output().cpu().numpy()
+            assert g.error() == 0
+            ref = np.stack([restatement.matvec_f16(w, ws, xq[t], xs[t], n, d, bits) for t in range(m)])
+            assert _same_bits(out, ref), call
+    finally:
+        g.close()
+
+
 def test_gather_rejections(mvb):
     import torch
     torch.cuda.set_device(0)
@@ -142,6 +175,28 @@ def _rank_main(rank, world, port, q):
             dist.barrier()  # no rank's kernel still writes into a buffer about to be freed
             g.close()
             dist.barrier()
+        # batch of 32 tokens through the tensor-core matmul, rows gathered by its epilogue
+        n, d, bits, m = 896, 1027, 4, 32
+        rng = np.random.default_rng(77)
+        w, ws = _random_q(rng, n, d, bits)
+        rows = -(-d // world)
+        w_blk, ws_blk = _shard(w, ws, rank, rows, d)
+        g = mvb.ShardGather(rank, world, rows, tokens=m)
+        handles = [None] * world
+        dist.all_gather_object(handles, g.handle())
+        g.connect(handles)
+        xq = rng.integers(-128, 128, (m, n)).astype(np.int8)
+        xs = rng.uniform(1e-3, 1e-1, (m, n // 32)).astype(np.float32)
+        xs_gm, ldx = _xs_group_major(xs, m)
+        g.gemm4(torch.from_numpy(w_blk).cuda(), torch.from_numpy(ws_blk.view(np.int16)).cuda(),
+                torch.from_numpy(xq).cuda(), torch.from_numpy(xs_gm).cuda(), n, m, ldx, bits)
+        out = g.output()[:, :d].cpu().numpy()
+        ref = np.stack([orc.matvec_f16(w, ws, xq[t], xs[t], n, d, bits) for t in range(m)])
+        results["batch32"] = bool(g.error() == 0 and _same_bits(out, ref))
+        torch.cuda.synchronize()
+        dist.barrier()
+        g.close()
+        dist.barrier()
         # A rank that skips a call: the other rank's bounded wait gives up and reports it.
         g = mvb.ShardGather(rank, world, 256)
         handles = [None] * world
