@@ -229,7 +229,7 @@ def our_arm(args, rank, world, local_rank):
     achieved = d["bytes"] / (d["ms"] / 1000.0) / 1e9
     mv_bytes = sum(kinds[k]["bytes"] for k in MATVEC_KINDS)
     mv_ms = sum(kinds[k]["ms"] for k in MATVEC_KINDS)
-    roofline = {"bound": "hbm", "kernel": f"fused_matvec ({dom})", "achieved": round(achieved, 1), "peak": peak,
+    roofline = {"bound": "hbm", "kernel": f"decode_matvec_kernel ({dom})", "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                 "traffic": None, "bytes_per_launch": round(d["bytes"] / d["launches"]),
                 "us_per_launch": round(1000.0 * d["ms"] / d["launches"], 3),
@@ -452,6 +452,31 @@ def prompt_mode(args):
                       "tok_s": round((PROMPT_LEN - 1) / ms * 1000, 1), "steps": args.steps, "warmup": args.warmup}))
 
 
+def step_mode(args):
+    """Config 3's decode alone, for profiling: load, batched prompt prefill, then K single decode steps (graph
+    launches) after W warm-up steps, each device-timed on the model's stream; prints the median step time."""
+    import torch
+    mvb = load_pkg()
+    torch.cuda.set_device(0)
+    dec = mvb.QwenDecoder(model_path(0, 1), ctx=512)
+    stream = torch.cuda.ExternalStream(dec.stream_handle)
+    prompt = prompt_ids()
+    dec.prefill(prompt)
+    dec.launch(args.warmup)
+    ts = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dec.launch(1)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    dec.close()
+    ms = statistics.median(ts)
+    print(json.dumps({"mode": "step", "ms_per_token": round(ms, 4), "tok_s": round(1000 / ms, 1),
+                      "steps": args.steps, "warmup": args.warmup}))
+
+
 def sharded_mode(args, rank, world, local_rank):
     """Config 5: one matrix row-sharded across the ranks (contiguous row blocks), each rank's matvec on its
     shard, and every rank ends the step holding the whole fp32 output. Two ways are timed per step with CUDA
@@ -587,9 +612,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
-    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill", "prompt"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill", "prompt", "step"],
                     help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "
-                         "prefill (tensor-core matmul over many tokens), prompt (batched prompt prefill)")
+                         "prefill (tensor-core matmul over many tokens), prompt (batched prompt prefill), "
+                         "step (single decode steps)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -605,6 +631,9 @@ def main():
         return
     if args.mode == "prompt":
         prompt_mode(args)
+        return
+    if args.mode == "step":
+        step_mode(args)
         return
     if world > 1:
         import datetime
