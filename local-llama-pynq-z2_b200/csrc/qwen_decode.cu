@@ -1,19 +1,20 @@
 // Device-resident Qwen2 decode over the group-quantized matvec (the reference's token loop, qwen/qwen.c:490-573
 // and :669-712, moved onto the B200 so the matvecs run back to back instead of one host round trip each).
 //
-// One forward step is a fixed sequence of kernels, captured once into a CUDA graph:
+// One forward step is a fixed sequence of 122 kernels (for 24 layers), captured once into a CUDA graph:
 //   embed                       x = dequantized embedding row of the current token          qwen.c:498-501
 //   per layer:
 //     qkv  (fused matvec)       rmsnorm(x) -> quantize -> [wq; wk; wv] rows, raw outputs     qwen.c:516-520
 //     attention (per q head)    + biases, NeoX RoPE, KV-cache write, softmax attention       qwen.c:521-546
 //     o    (fused matvec)       quantize(xb) -> wo, x += out                                 qwen.c:549-551
 //     gate/up (fused matvec)    rmsnorm(x) -> quantize -> w1, w3 rows paired, SwiGLU -> hb    qwen.c:554-562
-//     down (fused matvec)       quantize(hb) -> w2, x += out                                 qwen.c:563-565
-//   final norm + quantize       rmsnorm(x) -> xq, xs                                         qwen.c:569-570
-//   head (matvec)               Q8 head rows -> logits, block argmax -> atomicMax            qwen.c:571, 591-598
-//   next token                  prompt[pos+1] while feeding the prompt, else head_ids[argmax] qwen.c:677-683
+//     down (fused matvec)       quantize(hb) -> w2, x += out; after the last layer its last  qwen.c:563-565,
+//                               CTA also does the final rmsnorm + quantize                   :569-570
+//   head (matvec)               Q8 head rows -> logits, block argmax -> atomicMax; its last  qwen.c:571, 591-598,
+//                               CTA picks the next token (prompt[pos+1], else head_ids[argmax]) :677-683
 // The step reads the token and the position from device memory, so the same graph serves every position and
-// a whole generation is the graph launched once per position with no host work in between.
+// a whole generation is the graph launched once per position with no host work in between. The prompt is fed
+// in batches instead (prefill_batch: tensor-core matmuls, prefill_kernels.cuh), which writes the same KV cache.
 //
 // Arithmetic follows qwen.c operation by operation: no fused multiply-adds (the library is built with
 // -fmad=false and uses explicitly rounded intrinsics), sums in the reference's order (rmsnorm's sum of squares,
