@@ -341,9 +341,30 @@ def sweep_mode(args):
     peak, peak_kind = peaks()
     shapes = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 1152, 4), (896, 65536, 8),
               (896, 151936, 8), (8192, 131072, 4)]
+    # runq's int8 weights with fp32 scales (fpga_matvec): the stories15M / stories110M shapes, group size 32
+    runq_shapes = [(288, 288), (288, 768), (768, 288), (288, 32000), (768, 768), (768, 2048), (2048, 768),
+                   (768, 32000)]
     if args.only:
         shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+        runq_shapes = [sh for sh in runq_shapes if f"{sh[1]}x{sh[0]}" == args.only]
     out_lines = []
+    for n, d in runq_shapes:
+        gs = 32
+        b = _alg_bytes(n, d, 8, scale_bytes=4, gs=gs)
+        copies = max(2, min(4096, -(-300 * 2**20 // b)))
+        w = [torch.randint(-127, 128, (d * n,), dtype=torch.int8, device="cuda", generator=gen) for _ in range(copies)]
+        sc = [torch.rand(d * (n // gs), device="cuda", generator=gen) * 0.019 + 0.001 for _ in range(copies)]
+        xq = torch.randint(-127, 128, (n,), dtype=torch.int8, device="cuda", generator=gen)
+        xs = torch.rand(n // gs, device="cuda", generator=gen) * 0.05
+        out = torch.empty(d, device="cuda")
+        reps = max(copies, 64)
+        t = _time_graph(torch, lambda i: mvb.matvec(w[i % copies], sc[i % copies], xq, xs, out, n, d, gs), reps)
+        line = {"shape": f"{d}x{n} Q8 fp32-scale (runq)", "us": round(t * 1e6, 3), "GBps": round(b / t / 1e9, 1),
+                "frac": round(b / t / 1e9 / peak, 4), "bytes": b, "copies": copies}
+        out_lines.append(line)
+        print(json.dumps(line), flush=True)
+        del w, sc
+        torch.cuda.empty_cache()
     for n, d, bits in shapes:
         b = _alg_bytes(n, d, bits)
         copies = max(2, min(4096, -(-300 * 2**20 // b)))
