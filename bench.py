@@ -146,6 +146,44 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def step_roofline(dec, token, pos, reps=5):
+    """Per-kernel-kind device times of the decode step at (token, pos), from CUDA events around every kernel of the
+    instrumented step (mvb_qwen_profile, mean of `reps`), against the measured HBM peak: the dominant kind's
+    algorithmic GB/s and those of all matvecs together."""
+    import numpy as np
+    info = dec.kernel_info(pos)
+    runs = []
+    for _ in range(reps):
+        dec.rewind(token, pos, -1)
+        runs.append(dec.profile())
+    ms = np.mean(runs, axis=0)
+    kinds = {}
+    for (kind, layer, b), t in zip(info, ms):
+        k = kinds.setdefault(kind, {"launches": 0, "ms": 0.0, "bytes": 0.0})
+        k["launches"] += 1
+        k["ms"] += float(t)
+        k["bytes"] += b
+    step_ms = float(ms.sum())
+    dom = max(kinds, key=lambda k: kinds[k]["ms"])
+    peak, peak_kind = peaks()
+    d = kinds[dom]
+    achieved = d["bytes"] / (d["ms"] / 1000.0) / 1e9
+    mv_bytes = sum(kinds[k]["bytes"] for k in MATVEC_KINDS)
+    mv_ms = sum(kinds[k]["ms"] for k in MATVEC_KINDS)
+    label = {"attention": "attention_kernel", "embed": "embed_kernel"}.get(dom, "decode_matvec_kernel")
+    return {"bound": "hbm", "kernel": f"{label} ({dom})", "kind": dom, "achieved": round(achieved, 1), "peak": peak,
+            "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+            "traffic": None, "bytes_per_launch": round(d["bytes"] / d["launches"]),
+            "us_per_launch": round(1000.0 * d["ms"] / d["launches"], 3),
+            "step_share": round(d["ms"] / step_ms, 4),
+            "all_matvecs": {"bytes_per_token": round(mv_bytes), "ms_per_token": round(mv_ms, 4),
+                            "achieved": round(mv_bytes / (mv_ms / 1000.0) / 1e9, 1),
+                            "frac": round(mv_bytes / (mv_ms / 1000.0) / 1e9 / peak, 4)},
+            "instrumented_step_ms": round(step_ms, 4),
+            "per_kind": {k: {"launches": v["launches"], "us_per_launch": round(1000 * v["ms"] / v["launches"], 2),
+                             "GBps": round(v["bytes"] / (v["ms"] / 1000) / 1e9, 1)} for k, v in kinds.items()}}
+
+
 def our_arm(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -210,36 +248,8 @@ def our_arm(args, rank, world, local_rank):
     e2e = world * args.steps * GEN / t_e2e
     # roofline: one instrumented step at the middle decode position, 5 repeats
     mid = pos0 + GEN // 2
-    info = dec.kernel_info(mid)
-    reps = []
-    for _ in range(5):
-        dec.rewind(tok0 if mid == pos0 else int(ids_first[mid - pos0 - 1]), mid, -1)
-        reps.append(dec.profile())
-    ms = np.mean(reps, axis=0)
-    kinds = {}
-    for (kind, layer, b), t in zip(info, ms):
-        k = kinds.setdefault(kind, {"launches": 0, "ms": 0.0, "bytes": 0.0})
-        k["launches"] += 1
-        k["ms"] += float(t)
-        k["bytes"] += b
-    step_ms = float(ms.sum())
-    dom = max(kinds, key=lambda k: kinds[k]["ms"])
-    peak, peak_kind = peaks()
-    d = kinds[dom]
-    achieved = d["bytes"] / (d["ms"] / 1000.0) / 1e9
-    mv_bytes = sum(kinds[k]["bytes"] for k in MATVEC_KINDS)
-    mv_ms = sum(kinds[k]["ms"] for k in MATVEC_KINDS)
-    roofline = {"bound": "hbm", "kernel": f"decode_matvec_kernel ({dom})", "achieved": round(achieved, 1), "peak": peak,
-                "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": None, "bytes_per_launch": round(d["bytes"] / d["launches"]),
-                "us_per_launch": round(1000.0 * d["ms"] / d["launches"], 3),
-                "step_share": round(d["ms"] / step_ms, 4),
-                "all_matvecs": {"bytes_per_token": round(mv_bytes), "ms_per_token": round(mv_ms, 4),
-                                "achieved": round(mv_bytes / (mv_ms / 1000.0) / 1e9, 1),
-                                "frac": round(mv_bytes / (mv_ms / 1000.0) / 1e9 / peak, 4)},
-                "instrumented_step_ms": round(step_ms, 4),
-                "per_kind": {k: {"launches": v["launches"], "us_per_launch": round(1000 * v["ms"] / v["launches"], 2),
-                                 "GBps": round(v["bytes"] / (v["ms"] / 1000) / 1e9, 1)} for k, v in kinds.items()}}
+    roofline = step_roofline(dec, tok0 if mid == pos0 else int(ids_first[mid - pos0 - 1]), mid)
+    dom = roofline["kind"]
     traffic = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
     if os.path.exists(traffic):
         for line in open(traffic):
@@ -624,6 +634,144 @@ def sharded_mode(args, rank, world, local_rank):
                           "results": results}), flush=True)
 
 
+RUNQ_MODELS = {"stories15m": ("STORIES15M", "stories15M"), "stories110m": ("STORIES110M", "stories110M")}
+RUNQ_PROMPT = 4
+
+
+def run_reference_runq(path, prompt, npos, threads):
+    """runq.c's CPU build (oracle/_ref/libref_runq.so: its own forward) on the same checkpoint and prompt in a child
+    process with `threads` OpenMP threads: (tok/s over positions 1 .. npos-1, timed like runq.c:1024-1033 from the
+    end of the first forward, greedy ids after the prompt)."""
+    code = f"""
+import sys, time
+import numpy as np
+sys.path.insert(0, {os.path.join(ROOT, 'oracle')!r})
+import oracle
+r = oracle.RefRunq()
+r.open({path!r})
+prompt, tok, ids = {list(prompt)!r}, {int(prompt[0])}, []
+for pos in range({npos}):
+    lg = r.forward(tok, pos)
+    if pos == 0:
+        t0 = time.perf_counter()
+    tok = prompt[pos + 1] if pos + 1 < len(prompt) else int(r.lib.ref_runq_argmax(
+        lg.ctypes.data_as(oracle.C.POINTER(oracle.C.c_float)), lg.size))
+    if pos + 1 >= len(prompt):
+        ids.append(tok)
+print(({npos} - 1) / (time.perf_counter() - t0))
+print(",".join(map(str, ids)))
+"""
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=900)
+    if r.returncode != 0:
+        raise RuntimeError("reference runq failed: " + r.stderr[-500:])
+    out = r.stdout.strip().splitlines()
+    return float(out[0]), [int(t) for t in out[1].split(",") if t]
+
+
+def runq_mode(args):
+    """Configs 1 and 2: runq.c's int8 models (stories15M / stories110M architectures, synthetic seeded weights,
+    gs 32, shared classifier) decoded on the device (mvb_runq_load + the captured step graph). One step = the rest
+    of a 256-position run after the 4-token prompt (253 greedy tokens, positions 3 .. 255).
+      value        device time of K steps (rewind to position 3 + 253 graph launches), L2 warm: the model is smaller
+                   than the 126 MB L2, so a token's weights mostly stay there between tokens, as in a real decode
+      flushed      the same tokens timed one by one with a 256 MB L2 flush before each (outside the timed events)
+      e2e          mvb_runq_generate through the public API: prompt up, 253 ids back, host wall clock
+      cpu_baseline runq.c's CPU build on the same file and prompt, all host cores, 64 positions"""
+    import numpy as np
+    import torch
+    torch.cuda.set_device(0)
+    mvb = load_pkg()
+    sys.path.insert(0, PKG)
+    import qwb
+    names = [args.model] if args.model else list(RUNQ_MODELS)
+    peak, peak_kind = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for name in names:
+        cfg_name, arch = RUNQ_MODELS[name]
+        cfg = getattr(qwb, cfg_name)
+        path = os.path.join(DATA, f"{name}_s3.bin")
+        if not os.path.exists(path):
+            os.makedirs(DATA, exist_ok=True)
+            qwb.write_synthetic_runq(path + ".tmp", cfg, seed=3, gs=32)
+            os.replace(path + ".tmp", path)
+        prompt = [int(t) for t in np.random.default_rng(4).integers(3, cfg["vocab_size"], RUNQ_PROMPT)]
+        npos = 256
+        gen = npos - RUNQ_PROMPT + 1
+        t0 = time.perf_counter()
+        dec = mvb.RunqDecoder(path, ctx=cfg["seq_len"])
+        load_s = time.perf_counter() - t0
+        stream = torch.cuda.ExternalStream(dec.stream_handle)
+        pos0, tok0 = RUNQ_PROMPT - 1, prompt[-1]
+        dec.prefill(prompt)
+        ids_ref = dec.decode(gen)
+
+        def steps(k):
+            for _ in range(k):
+                dec.rewind(tok0, pos0, RUNQ_PROMPT)
+                dec.launch(gen)
+        steps(args.warmup)
+        torch.cuda.synchronize()
+        clocks = Clocks(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        steps(args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        t_dev = e0.elapsed_time(e1) / 1000.0
+        value = args.steps * gen / t_dev
+        # flushed: token by token, an L2-sized write before each (on the model's stream, outside the events)
+        dec.rewind(tok0, pos0, RUNQ_PROMPT)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(gen)]
+        with torch.cuda.stream(stream):
+            for a, b in ev:
+                flush.fill_(1)
+                a.record(stream)
+                dec.launch(1)
+                b.record(stream)
+        torch.cuda.synchronize()
+        t_flush = sum(a.elapsed_time(b) for a, b in ev) / 1000.0
+        # e2e through the public API
+        ts = []
+        for _ in range(max(1, min(args.steps, 5))):
+            t0 = time.perf_counter()
+            ids = dec.generate(prompt, gen)
+            ts.append(time.perf_counter() - t0)
+        t_e2e = statistics.median(ts)
+        stop = ids_ref.tolist().index(1) if 1 in ids_ref.tolist() else gen
+        if ids.tolist() != ids_ref.tolist()[:stop]:
+            raise RuntimeError("generate disagrees with the decode steps")
+        roof = step_roofline(dec, int(ids_ref[gen // 2 - 1]), pos0 + gen // 2)
+        kernels = dec.cfg["kernels_per_step"]
+        dec.close()
+        cpu = None
+        if not args.no_cpu_baseline and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libref_runq.so")):
+            threads = os.cpu_count()
+            sample_pos = 64
+            tps, ref_ids = run_reference_runq(path, prompt, sample_pos, threads)
+            cpu = {"value": round(tps, 2), "unit": "tok/s", "cores": threads, "kind": "reference",
+                   "sample": f"runq.c CPU build (-O3 -fopenmp -ffp-contract=off) forward() on the same file and "
+                             f"prompt, {sample_pos} positions, tok/s from the end of the first forward as runq.c "
+                             f"reports it",
+                   "same_ids_as_b200": ref_ids == ids_ref.tolist()[:len(ref_ids)]}
+        line = {"mode": "runq", "metric": f"runq int8 decode tok/s ({arch} arch, 1 B200)", "value": round(value, 1),
+                "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(1000.0 * t_dev / args.steps, 4),
+                "us_per_token": round(1e6 * t_dev / args.steps / gen, 2),
+                "higher_is_better": True, "dtype": "int8->int32, fp32", "data": "synthetic",
+                "config": {"workload": f"{arch} architecture via runq (synthetic seeded runq v2 Q8_0, gs 32, shared "
+                                       f"classifier), 4-token prompt, {gen} greedy tokens per step", "model": cfg,
+                           "l2": "warm (weights fit in the 126 MB L2); 'flushed' gives the L2-flushed figure"},
+                "flushed": {"value": round(gen / t_flush, 1), "unit": "tok/s",
+                            "how": "each token timed alone after a 256 MB write to a scratch buffer"},
+                "e2e": {"value": round(gen / t_e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * RUNQ_PROMPT + 32,
+                        "d2h_bytes_per_step": 4 * gen + 32, "includes": "prompt feed (3 positions)"},
+                "roofline": roof, "cpu_baseline": cpu, "gpu_launches": args.steps * gen * kernels,
+                "kernels_per_token": kernels, "load_s": round(load_s, 3), "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -633,10 +781,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
-    ap.add_argument("--mode", default="decode", choices=["decode", "sweep", "sharded", "prefill", "prompt", "step"],
+    ap.add_argument("--model", default="", choices=["", *RUNQ_MODELS], help="runq: only this model")
+    ap.add_argument("--mode", default="decode",
+                    choices=["decode", "sweep", "sharded", "prefill", "prompt", "step", "runq"],
                     help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "
                          "prefill (tensor-core matmul over many tokens), prompt (batched prompt prefill), "
-                         "step (single decode steps)")
+                         "step (single decode steps), runq (configs 1 and 2: stories15M / stories110M decode)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -655,6 +805,9 @@ def main():
         return
     if args.mode == "step":
         step_mode(args)
+        return
+    if args.mode == "runq":
+        runq_mode(args)
         return
     if world > 1:
         import datetime

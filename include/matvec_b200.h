@@ -42,10 +42,14 @@ int mvb_qmatvec(const void *wq, const void *ws, const float *x, float *out, int 
 int mvb_rows_per_tile(int n, int d);
 
 
-/* ---- Device-resident Qwen2 decode (the reference's token loop, qwen/qwen.c:490-712, on the device) ----
+/* ---- Device-resident decode (the reference's token loops, qwen/qwen.c:490-712 and runq/runq.c:477-1026, on
+ * the device) ----
  * The whole forward step (embedding, per-layer rmsnorm/quantize/matvecs/attention/SwiGLU, head, greedy argmax)
  * runs on the current CUDA device as one captured CUDA graph, every matvec being this library's kernel. Token
  * and position live in device memory, so a generation is one graph launch per position with no host work.
+ * Two loaders make a decoder handle: mvb_qwen_load (a .qwb model, qwen.c's arithmetic) and mvb_runq_load (a runq
+ * version 2 checkpoint, runq.c's arithmetic). Every mvb_qwen_* call below takes either handle; "head" means
+ * qwen.c's trimmed head or runq.c's classifier (head_k = vocab_size rows, the row being the token id).
  * All calls below are synchronous except mvb_qwen_rewind and mvb_qwen_launch, and wait at most
  * MATVEC_TIMEOUT_S (default 5 s) plus 10 ms per position. */
 
@@ -53,6 +57,19 @@ int mvb_rows_per_tile(int n, int d);
  * captures the decode step; ctx is the KV-cache length (clipped to the header's max_seq_len like qwen.c:325,
  * at most 8192). Returns a handle, or NULL with the reason in mvb_last_error(). */
 void *mvb_qwen_load(const void *qwb_image, size_t bytes, int ctx);
+
+/* mvb_qwen_load of the .qwb file at `path`, mapped read-only and uploaded from the page cache (no host copy). */
+void *mvb_qwen_load_file(const char *path, int ctx);
+
+/* Loads a runq version 2 checkpoint (the whole file's bytes, runq.c:318-357: int8 weights with fp32 scales,
+ * shared or separate classifier) to the current device, each tensor in its own aligned slot, and captures the
+ * decode step with runq.c's arithmetic (its quantize, rmsnorm eps 1e-5, interleaved RoPE, no biases, greedy
+ * argmax over the classifier). Needs group size 32 and head size 32, 48 or 64 (group size 64 models run through
+ * fpga_matvec). ctx is clipped to the header's seq_len. Returns a decoder handle, or NULL with the reason. */
+void *mvb_runq_load(const void *checkpoint, size_t bytes, int ctx);
+
+/* mvb_runq_load of the checkpoint file at `path`, mapped read-only (no host copy). */
+void *mvb_runq_load_file(const char *path, int ctx);
 
 /* out[0..8] = dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, head_k, ctx, kernels per step. */
 int mvb_qwen_config(void *model, int *out);
@@ -68,7 +85,7 @@ int mvb_qwen_forward(void *model, int token, int pos, float *logits);
  * qwen.c generate() before its first sampled token. The fed tokens run through the layers in batches of up to 256
  * with the tensor-core matmul (mvb_gemm4) and a batched causal attention, writing the KV-cache rows one decode
  * step per token would write, bit for bit (qwen.c computes the logits of prompt positions and discards them;
- * this skips the head there). 0, or -1. */
+ * this skips the head there). A runq handle takes one decode step per fed token. 0, or -1. */
 int mvb_qwen_prefill(void *model, const int *prompt, int n);
 
 /* mvb_qwen_prefill's result reached one decode step per fed token (the reference's order of work). 0, or -1. */
@@ -82,8 +99,13 @@ int mvb_qwen_cache(void *model, int positions, float *k, float *v);
 int mvb_qwen_decode(void *model, int steps, int *ids);
 
 /* qwen.c generate() at -t 0 (qwen.c:669-712): prefill, then greedy ids into ids (host) until `steps`, a stop
- * token (<|im_end|>, <|endoftext|>, not copied) or a full context. Returns the number of ids, or -1. */
+ * token (<|im_end|>, <|endoftext|>, not copied) or a full context. Returns the number of ids, or -1. For a runq
+ * handle this is runq.c generate() at -t 0 (runq.c:982-1026), whose stop token is BOS = 1. */
 int mvb_qwen_generate(void *model, const int *prompt, int n_prompt, int steps, int *ids);
+
+/* The same call under runq's name. runq.c's `-n steps` counts positions from 0, so it samples
+ * steps - n_prompt + 1 tokens: pass that as `steps` here for the same run. */
+int mvb_runq_generate(void *model, const int *prompt, int n_prompt, int steps, int *ids);
 
 /* Sets the state to input `token` at position `pos` (positions below keep their KV cache), with n_prompt the
  * prompt length for the prompt/greedy switch (negative: no sampling). Asynchronous on the model's stream (the

@@ -60,8 +60,12 @@ def lib():
         L.mvb_rows_per_tile.restype = i
         L.mvb_rows_per_tile.argtypes = [i, i]
         ip = C.POINTER(C.c_int)
-        L.mvb_qwen_load.restype = vp
-        L.mvb_qwen_load.argtypes = [vp, C.c_size_t, i]
+        for name in ("mvb_qwen_load", "mvb_runq_load"):
+            getattr(L, name).restype = vp
+            getattr(L, name).argtypes = [vp, C.c_size_t, i]
+        for name in ("mvb_qwen_load_file", "mvb_runq_load_file"):
+            getattr(L, name).restype = vp
+            getattr(L, name).argtypes = [C.c_char_p, i]
         L.mvb_qwen_config.restype = i
         L.mvb_qwen_config.argtypes = [vp, ip]
         L.mvb_qwen_stream.restype = vp
@@ -76,8 +80,9 @@ def lib():
         L.mvb_qwen_cache.argtypes = [vp, i, C.POINTER(C.c_float), C.POINTER(C.c_float)]
         L.mvb_qwen_decode.restype = i
         L.mvb_qwen_decode.argtypes = [vp, i, ip]
-        L.mvb_qwen_generate.restype = i
-        L.mvb_qwen_generate.argtypes = [vp, ip, i, i, ip]
+        for name in ("mvb_qwen_generate", "mvb_runq_generate"):
+            getattr(L, name).restype = i
+            getattr(L, name).argtypes = [vp, ip, i, i, ip]
         L.mvb_qwen_rewind.restype = i
         L.mvb_qwen_rewind.argtypes = [vp, i, i, i]
         L.mvb_qwen_launch.restype = i
@@ -331,18 +336,22 @@ class ShardGather:
 # ---- device-resident Qwen2 decode (include/matvec_b200.h, mvb_qwen_*) ----
 
 class QwenDecoder:
-    """A .qwb model resident on the current CUDA device, decoding through the captured step graph."""
+    """A .qwb model resident on the current CUDA device, decoding through the captured step graph. A path is
+    mapped and uploaded by the library itself (mvb_qwen_load_file); bytes go through mvb_qwen_load."""
+
+    _load, _load_file = "mvb_qwen_load", "mvb_qwen_load_file"
 
     def __init__(self, path_or_bytes, ctx=1024):
         import numpy as np
         if isinstance(path_or_bytes, (bytes, bytearray, memoryview)):
             img = np.frombuffer(path_or_bytes, np.uint8)
+            h = getattr(lib(), self._load)(img.ctypes.data, img.nbytes, ctx)
+            who = self._load
         else:
-            img = np.fromfile(path_or_bytes, np.uint8)
-        self._img = img
-        h = lib().mvb_qwen_load(img.ctypes.data, img.nbytes, ctx)
+            h = getattr(lib(), self._load_file)(os.fsencode(path_or_bytes), ctx)
+            who = self._load_file
         if not h:
-            raise MatvecError("mvb_qwen_load failed: " + last_error())
+            raise MatvecError(who + " failed: " + last_error())
         self.h = h
         cfg = (C.c_int * 9)()
         lib().mvb_qwen_config(h, cfg)
@@ -447,3 +456,11 @@ class QwenDecoder:
             self.close()
         except Exception:
             pass
+
+
+class RunqDecoder(QwenDecoder):
+    """A runq version 2 checkpoint (runq/runq.c's int8 model) resident on the current CUDA device, decoding with
+    runq.c's arithmetic through the same captured step graph and the same calls (mvb_runq_load*). ``head_k`` is
+    the vocabulary (the classifier's row is the token id), and generate() stops at BOS = 1 like runq.c:1016."""
+
+    _load, _load_file = "mvb_runq_load", "mvb_runq_load_file"

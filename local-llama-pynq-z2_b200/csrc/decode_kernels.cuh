@@ -8,7 +8,12 @@
 //      done. Two kernels also have a tail run by their last CTA to finish (an atomic counter that this CTA
 //      resets for the next step): the last layer's down projection normalizes x once for the 2,048-CTA head,
 //      and the head picks the next token.
-// The arithmetic of every step is qwen.c's, operation by operation (see qwen_decode.cu).
+// The kernels serve two model families, chosen by the template parameter FAM:
+//   kQwen  qwen.c (qwen/qwen.c): int4/int8 weights with fp16 scales, activations quantized by the reciprocal of
+//          the scale, q/k/v biases, NeoX RoPE (pairs i, i + hs/2), a head mapped through head_ids;
+//   kRunq  runq.c (runq/runq.c): int8 weights with fp32 scales, activations quantized by dividing by the scale,
+//          no biases, interleaved RoPE (pairs 2i, 2i + 1), the classifier's row is the token.
+// The arithmetic of every step is the family's reference, operation by operation (see qwen_decode.cu).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -17,7 +22,10 @@
 #include "matvec_kernels.cuh"
 
 namespace mvb {
-namespace qwen {
+namespace decode {
+
+// model families; the values are the matching activation-quantization modes of matvec_kernels.cuh
+constexpr int kQwen = kXQuantizeQwen, kRunq = kXQuantizeRunq;
 
 constexpr int kImEnd = 151645, kEndOfText = 151643;  // qwen.c:31-32
 constexpr int kMaxNormPerThread = 8;                     // rmsnorm'd vectors have at most 8 * 256 = 2048 elements
@@ -34,12 +42,13 @@ struct State {
 
 __device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 
-// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of 32 like qwen.c:355-364 into a CTA's
-// activation planes (matvec_kernels.cuh layout: for int4 weights even/odd element planes, for int8 weights chunk
-// planes) and the scales into xs. Eight threads share a group, four consecutive elements each, so one pass of the
-// CTA covers 32 groups. The group maximum is taken over the float bits of |v| (order-free and exact; NaN counts
-// as 0, since qwen.c's fmaxf ignores NaN), combined across the eight threads with three shuffles.
-template <int BITS>
+// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of 32 like qwen.c:355-364 (FAM kQwen) or
+// runq.c:244-270 (kRunq) into a CTA's activation planes (matvec_kernels.cuh layout: for int4 weights even/odd
+// element planes, for int8 weights chunk planes) and the scales into xs. Eight threads share a group, four
+// consecutive elements each, so one pass of the CTA covers 32 groups. The group maximum is taken over the float
+// bits of |v| (order-free and exact; NaN counts as 0, since qwen.c's fmaxf and runq.c's `>` ignore NaN),
+// combined across the eight threads with three shuffles.
+template <int BITS, int FAM>
 __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs) {
     const int ng = n / 32, l = threadIdx.x & 7;
     for (int base = 0; base < ng; base += kThreads / 8) {  // the same trip count in every thread (shuffles)
@@ -55,12 +64,22 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        const float scale = __fmul_rn(__uint_as_float(m), 1.0f / 127.0f);
-        const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, same value
-        const uint32_t q0 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.x, inv)));
-        const uint32_t q1 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.y, inv)));
-        const uint32_t q2 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.z, inv)));
-        const uint32_t q3 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.w, inv)));
+        float scale;
+        uint32_t q0, q1, q2, q3;
+        if (FAM == kRunq) {  // runq.c: scale = wmax / 127, q = round(x / scale), no guard for a zero scale
+            scale = __fdiv_rn(__uint_as_float(m), 127.0f);
+            q0 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.x, scale)));
+            q1 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.y, scale)));
+            q2 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.z, scale)));
+            q3 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.w, scale)));
+        } else {
+            scale = __fmul_rn(__uint_as_float(m), 1.0f / 127.0f);
+            const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, same value
+            q0 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.x, inv)));
+            q1 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.y, inv)));
+            q2 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.z, inv)));
+            q3 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.w, inv)));
+        }
         if (on) {
             if (BITS == 4) {
                 // elements 4l, 4l+2 are even-plane bytes 2l, 2l+1; elements 4l+1, 4l+3 odd-plane bytes 2l, 2l+1
@@ -76,11 +95,13 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
     }
 }
 
-// Quantizes v[0 .. n-1] (shared memory) per group of 32 like qwen.c:355-364 into xq/xs (global); whole CTA.
+// Quantizes v[0 .. n-1] (shared memory) per group of 32 like qwen.c:355-364 (FAM kQwen) or runq.c:244-270
+// (kRunq) into xq/xs (global); whole CTA.
+template <int FAM>
 __device__ __forceinline__ void quantize_to_global(const float *v, int n, int8_t *xq, float *xs) {
     for (int g = threadIdx.x; g < n / 32; g += blockDim.x) {
         int8_t q[32];
-        xs[g] = quantize_group<32>(v, g, kXQuantizeQwen, q);
+        xs[g] = quantize_group<32>(v, g, FAM, q);
         uint32_t w[8];
 #pragma unroll
         for (int j = 0; j < 8; j++)
@@ -92,8 +113,9 @@ __device__ __forceinline__ void quantize_to_global(const float *v, int n, int8_t
     }
 }
 
-// rmsnorm (qwen.c:337-344) of xv (shared memory, n floats) with weight w, then quantize into xq/xs; whole CTA.
-// xb is n floats of shared scratch.
+// rmsnorm (qwen.c:337-344; runq.c:394-407 is the same sequence) of xv (shared memory, n floats) with weight w,
+// then quantize into xq/xs; whole CTA. xb is n floats of shared scratch.
+template <int FAM>
 __device__ __forceinline__ void rmsnorm_quantize(const float *xv, float *xb, const float *w, float eps, int n,
                                                  int8_t *xq, float *xs) {
     __shared__ float s_inv;
@@ -110,7 +132,7 @@ __device__ __forceinline__ void rmsnorm_quantize(const float *xv, float *xb, con
     const float s = s_inv;
     for (int j = threadIdx.x; j < n; j += blockDim.x) xb[j] = __fmul_rn(w[j], __fmul_rn(s, xv[j]));
     __syncthreads();
-    quantize_to_global(xb, n, xq, xs);
+    quantize_to_global<FAM>(xb, n, xq, xs);
 }
 
 // Once every CTA of the grid has called this (after its global writes), returns true in exactly one CTA: the
@@ -128,16 +150,20 @@ __device__ __forceinline__ bool last_cta(int *counter) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// embedding row of the current token (qwen.c:498-501), exact in fp32; also clears the head's argmax key.
-__global__ void embed_kernel(const int8_t *emb_q, const uint16_t *emb_s, float *x, int dim, State *st) {
+// embedding row of the current token (qwen.c:498-501 with fp16 scales, runq.c:490-492 with fp32 scales), exact in
+// fp32; also clears the head's argmax key.
+template <int FAM>
+__global__ void embed_kernel(const int8_t *emb_q, const void *emb_s, float *x, int dim, State *st) {
     allow_consumer();
     wait_for_producer();
     const int tok = __ldcg(&st->token);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i == 0) st->key = 0ull;
     if (i < dim) {
-        const size_t r = (size_t)tok * dim;
-        x[i] = __fmul_rn(__int2float_rn(emb_q[r + i]), scale_from_f16(emb_s[r / 32 + i / 32]));
+        const size_t r = (size_t)tok * dim, g = (r + i) / 32;
+        const float s = FAM == kRunq ? static_cast<const float *>(emb_s)[g]
+                                     : scale_from_f16(static_cast<const uint16_t *>(emb_s)[g]);
+        x[i] = __fmul_rn(__int2float_rn(emb_q[r + i]), s);
     }
 }
 
@@ -145,8 +171,9 @@ __global__ void embed_kernel(const int8_t *emb_q, const uint16_t *emb_s, float *
 enum Epilogue : int {
     kEpiStore = 0,     // out[row] = v
     kEpiResidual = 1,  // out[row] += v                                              (qwen.c:551, :565)
-    kEpiSwiGLU = 2,    // tile = rows of w1 then the same rows of w3; out[row] = silu(g) * u   (qwen.c:558-562)
-    kEpiHead = 3,      // out[row] = v, plus the argmax key                           (qwen.c:571, 591-598)
+    kEpiSwiGLU = 2,    // tile = rows of w1 then the same rows of w3; out[row] = silu(g) * u   (qwen.c:558-562,
+                       //                                                                      runq.c:588-596)
+    kEpiHead = 3,      // out[row] = v, plus the argmax key                 (qwen.c:571, 591-598; runq.c:843-854)
 };
 
 enum Prologue : int {
@@ -158,12 +185,13 @@ enum Prologue : int {
 enum Tail : int {
     kTailNone = 0,
     kTailNormQuant = 1,  // rmsnorm(out) + quantize into tail_xq/xs               (qwen.c:569-570)
-    kTailNextToken = 3,  // the prompt's next token or head_ids[argmax]            (qwen.c:677-683)
+    kTailNextToken = 3,  // the prompt's next token, else head_ids[argmax] (qwen.c:677-683) or the argmax row
+                         // itself when there are no head_ids (runq.c:1006-1012)
 };
 
 struct DecodeParams {
     const uint8_t *w[3];
-    const uint16_t *ws[3];
+    const void *ws[3];  // fp16 (kQwen) or fp32 (kRunq) scales
     int rows[3];        // rows of each matrix; the output row space is their concatenation (or the pair)
     int n, rt, d;       // columns, output rows per tile, output rows in total
     const int8_t *xq;   // quantized input (n) and its scales (n/32) (kProQuantized)
@@ -179,13 +207,14 @@ struct DecodeParams {
     int8_t *tail_xq;
     float *tail_xs;
     const int *prompt;
-    const int32_t *head_ids;
+    const int32_t *head_ids;  // null: the argmax row is the token
     int *ids;
     int cap;
 };
 
-template <int BITS, int EPI, int PRO, int TAIL, int UPT>
+template <int BITS, int FAM, int EPI, int PRO, int TAIL, int UPT>
 __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodeParams p) {
+    static_assert(FAM == kQwen || BITS == 8, "runq weights are int8");
     constexpr int GB = BITS == 4 ? 16 : 32;
     constexpr int WC = GB / 16;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -197,7 +226,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
 
     // 1. this tile's weights and scales into registers: they do not depend on any earlier kernel
     uint4 wv[UPT][WC];
-    uint32_t hs[UPT];
+    uint32_t hs[UPT];  // the scale's bits: fp16 (kQwen) or fp32 (kRunq), converted where it is used
 #pragma unroll
     for (int k = 0; k < UPT; k++) {
         const int u = tid + k * kThreads;
@@ -214,11 +243,12 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                 if (m == 1 && r >= p.rows[1]) { r -= p.rows[1]; m = 2; }
             }
             const uint8_t *wb = m == 0 ? p.w[0] : (m == 1 ? p.w[1] : p.w[2]);
-            const uint16_t *sb = m == 0 ? p.ws[0] : (m == 1 ? p.ws[1] : p.ws[2]);
+            const void *sb = m == 0 ? p.ws[0] : (m == 1 ? p.ws[1] : p.ws[2]);
             const size_t idx = (size_t)r * ng + g;
 #pragma unroll
             for (int c = 0; c < WC; c++) wv[k][c] = ld_weights(wb + idx * GB + 16 * c);
-            hs[k] = ld_u16(sb + idx);
+            hs[k] = FAM == kRunq ? __float_as_uint(ld_f32(static_cast<const float *>(sb) + idx))
+                                 : ld_u16(static_cast<const uint16_t *>(sb) + idx);
         }
     }
     // the rmsnorm weights this thread applies (constants), also before the wait
@@ -264,12 +294,13 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         // addressed from the shared array itself so that every access compiles to a shared-memory load (a
         // pointer that went through an integer cast would be generic, and the in-order sum would run at the
         // generic load's latency)
-        const size_t stage = (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
+        const size_t stage =
+            (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
         float *xv = reinterpret_cast<float *>(smem + ((stage + 15) & ~(size_t)15));
         for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
         __syncthreads();
         const float *qsrc = xv;
-        if (PRO == kProNorm) {  // qwen.c:337-344
+        if (PRO == kProNorm) {  // qwen.c:337-344, runq.c:394-407
             float *xn = xv + n;
             __shared__ float s_inv;
             for (int j = tid; j < n; j += kThreads) xn[j] = __fmul_rn(xv[j], xv[j]);
@@ -290,7 +321,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             __syncthreads();
             qsrc = xn;
         }
-        quantize_to_planes<BITS>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
+        quantize_to_planes<BITS, FAM>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
     }
     __syncthreads();
     if (BITS == 4) {
@@ -338,7 +369,8 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                     acc = __dp4a((int)wv[k][c].w, (int)a.w, acc);
                 }
             }
-            prod[vr * ps + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), scale_from_f16(hs[k])), xs_s[g]);
+            const float wscale = FAM == kRunq ? __uint_as_float(hs[k]) : scale_from_f16(hs[k]);
+            prod[vr * ps + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), wscale), xs_s[g]);
         }
     }
     __syncthreads();
@@ -363,7 +395,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         if (tid < rows) {
             float gv = prod[tid];
             const float u = prod[rows + tid];
-            gv = __fmul_rn(gv, __frcp_rn(__fadd_rn(1.0f, expf_ref(-gv, p.et))));  // 1.0f / (...) of qwen.c
+            gv = __fmul_rn(gv, __frcp_rn(__fadd_rn(1.0f, expf_ref(-gv, p.et))));  // 1.0f / (...) of both
             p.out[row0 + tid] = __fmul_rn(gv, u);
         }
     } else {  // kEpiHead
@@ -388,12 +420,12 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     float *sm = reinterpret_cast<float *>(smem);
     if (TAIL == kTailNormQuant) {
         for (int j = tid; j < p.d / 4; j += kThreads) reinterpret_cast<float4 *>(sm)[j] = ld_cg4(p.out + 4 * j);
-        rmsnorm_quantize(sm, sm + p.d, p.tail_norm, p.eps, p.d, p.tail_xq, p.tail_xs);
+        rmsnorm_quantize<FAM>(sm, sm + p.d, p.tail_norm, p.eps, p.d, p.tail_xq, p.tail_xs);
     } else if (TAIL == kTailNextToken && tid == 0) {
         State *st = p.st;
         const int pos = st->pos;
         const unsigned long long key = atomicAdd(&st->key, 0ull);
-        // no key: every logit was NaN; the reference's strict `>` then keeps row 0 (qwen.c:591-598)
+        // no key: every logit was NaN; the reference's strict `>` then keeps row 0 (qwen.c:591-598, runq.c:843-854)
         const int row = key ? (int)(~(uint32_t)(key & 0xffffffffu)) : 0;
         st->last_row = row;
         if (st->n_prompt >= 0) {
@@ -401,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             if (pos + 1 < st->n_prompt) {
                 next = p.prompt[pos + 1];
             } else {
-                next = p.head_ids[row];
+                next = p.head_ids ? p.head_ids[row] : row;
                 if (st->n_gen < p.cap) p.ids[st->n_gen] = next;
                 st->n_gen++;
             }
@@ -423,16 +455,17 @@ inline size_t decode_smem_bytes(int n, int rt, int epi, int pro, int tail, int d
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// attention for one query head (qwen.c:521-546): biases, NeoX RoPE (pairs i, i + hs/2), the KV-cache write of
-// this position, scores q.k / sqrt(hs) in order over the head's elements, softmax in order, weighted values in
-// order of position. The cached values of this head's kv head are staged in shared memory (cp.async, double
-// buffered in chunks of kVChunk positions) while the scores are computed. The last CTA quantizes the output.
+// attention for one query head (qwen.c:521-546; runq.c:506-567): the biases and NeoX RoPE (pairs i, i + hs/2) of
+// qwen.c, or runq.c's interleaved RoPE (pairs 2i, 2i + 1) without biases; the KV-cache write of this position,
+// scores q.k / sqrt(hs) in order over the head's elements, softmax in order, weighted values in order of position.
+// The cached values of this head's kv head are staged in shared memory (cp.async, double buffered in chunks of
+// kVChunk positions) while the scores are computed.
 constexpr int kVChunk = 256;
 
 struct AttnParams {
     const float *qkv;   // raw outputs of the qkv matvec: q (dim) | k (kv_dim) | v (kv_dim)
-    const float *bq, *bk, *bv;
-    const float *rope;  // per position: cos[hs/2] then sin[hs/2]
+    const float *bq, *bk, *bv;  // kQwen only
+    const float *rope;  // per position: cos[hs/2] then sin[hs/2] of each rotated pair
     float *kcache, *vcache;  // this layer's (ctx, kv_dim)
     float *xb;          // dim outputs
     int dim, kv_dim, kv_mul, ctx;
@@ -489,7 +522,7 @@ __device__ __forceinline__ float weighted_chain(float acc, const float *a, const
     return acc;
 }
 
-template <int HS>
+template <int HS, int FAM>
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p) {
     extern __shared__ __align__(16) float asm_[];
     float *q = asm_, *kc = q + HS, *vc = kc + HS;
@@ -513,29 +546,36 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         for (int i = 0; i < HS / 4; i++) k4[i] = ld_cg4(kt + 4 * i);
     }
     const float *cs = p.rope + (size_t)pos * HS;
+    // this thread's rotated pair (i0, i1): NeoX halves for qwen.c, neighbours for runq.c
+    const int i0 = FAM == kRunq ? 2 * tid : tid, i1 = FAM == kRunq ? 2 * tid + 1 : tid + half;
     float rc = 0.0f, rs = 0.0f, bq0 = 0.0f, bq1 = 0.0f, bk0 = 0.0f, bk1 = 0.0f, bv0 = 0.0f;
     if (tid < half) {
         rc = cs[tid];
         rs = cs[half + tid];
-        bq0 = p.bq[h * HS + tid];
-        bq1 = p.bq[h * HS + tid + half];
-        bk0 = p.bk[kvh * HS + tid];
-        bk1 = p.bk[kvh * HS + tid + half];
+        if (FAM == kQwen) {
+            bq0 = p.bq[h * HS + i0];
+            bq1 = p.bq[h * HS + i1];
+            bk0 = p.bk[kvh * HS + i0];
+            bk1 = p.bk[kvh * HS + i1];
+        }
     }
-    if (tid < HS) bv0 = p.bv[kvh * HS + tid];
+    if (FAM == kQwen && tid < HS) bv0 = p.bv[kvh * HS + tid];
     wait_for_producer();
     const float *qr = p.qkv + h * HS, *kr = p.qkv + p.dim + kvh * HS, *vr = p.qkv + p.dim + p.kv_dim + kvh * HS;
+    // qwen.c adds the biases to the raw outputs (qwen.c:521-524); runq.c rotates them as they are (runq.c:506-521)
+    auto in = [](const float *r, int i, float bias) {
+        return FAM == kQwen ? __fadd_rn(__ldcg(r + i), bias) : __ldcg(r + i);
+    };
     if (tid < half) {
-        float a = __fadd_rn(__ldcg(qr + tid), bq0);
-        float b = __fadd_rn(__ldcg(qr + tid + half), bq1);
-        q[tid] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
-        q[tid + half] = __fadd_rn(__fmul_rn(b, rc), __fmul_rn(a, rs));
-        a = __fadd_rn(__ldcg(kr + tid), bk0);
-        b = __fadd_rn(__ldcg(kr + tid + half), bk1);
-        kc[tid] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
-        kc[tid + half] = __fadd_rn(__fmul_rn(b, rc), __fmul_rn(a, rs));
+        float a = in(qr, i0, bq0), b = in(qr, i1, bq1);
+        q[i0] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
+        q[i1] = __fadd_rn(__fmul_rn(b, rc), __fmul_rn(a, rs));
+        a = in(kr, i0, bk0);
+        b = in(kr, i1, bk1);
+        kc[i0] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
+        kc[i1] = __fadd_rn(__fmul_rn(b, rc), __fmul_rn(a, rs));
     }
-    if (tid < HS) vc[tid] = __fadd_rn(__ldcg(vr + tid), bv0);
+    if (tid < HS) vc[tid] = in(vr, tid, bv0);
     __syncthreads();
     if (h % p.kv_mul == 0 && tid < HS) {  // one writer per kv head
         p.kcache[(size_t)pos * p.kv_dim + kvh * HS + tid] = kc[tid];
@@ -563,7 +603,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         att[t] = __fdiv_rn(score, scale);
     }
     __syncthreads();
-    // softmax (qwen.c:346-352): max, exp(x - max), in-order sum, divide
+    // softmax (qwen.c:346-352, runq.c:409-427): max, exp(x - max), in-order sum, divide
     float m = -INFINITY;
     for (int t = tid; t <= pos; t += kThreads) m = fmaxf(m, att[t]);
 #pragma unroll
@@ -611,5 +651,5 @@ inline size_t attention_smem_bytes(int ctx) {
     return (size_t)3 * HS * 4 + (size_t)((ctx + 3) & ~3) * 4 + (size_t)2 * kVChunk * HS * 4;
 }
 
-}  // namespace qwen
+}  // namespace decode
 }  // namespace mvb

@@ -15,7 +15,7 @@
 #include "matvec_kernels.cuh"
 
 namespace mvb {
-namespace qwen {
+namespace decode {
 
 // Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of 32 like qwen.c:355-364 into xq (element
 // order) and xs[g * ldx]; the operations of quantize_to_planes, with eight threads per group. Whole CTA of
@@ -227,5 +227,5 @@ inline size_t attention_rows_smem_bytes(int npos, int vchunk) {
     return (size_t)HS * 4 + (size_t)((npos + 3) & ~3) * 4 + (size_t)vchunk * HS * 4;
 }
 
-}  // namespace qwen
+}  // namespace decode
 }  // namespace mvb

@@ -26,7 +26,11 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
 #include <time.h>
+#include <unistd.h>
 
 #include <map>
 #include <mutex>
@@ -40,7 +44,7 @@
 #include "mvb_runtime.h"
 
 namespace mvb {
-namespace qwen {
+namespace decode {
 
 constexpr int kMaxDim = 2048;     // largest dim the norm kernels stage in shared memory
 constexpr int kMaxCtx = 8192;     // largest context (attention scores live in shared memory)
@@ -100,20 +104,22 @@ struct Config {
 
 struct Mat {
     const uint8_t *w;
-    const uint16_t *s;
+    const void *s;  // fp16 scales (kQwen) or fp32 scales (kRunq), one per group of 32
 };
 
 struct Model {
     Config c;
+    int family = kQwen;  // kQwen: a .qwb model for qwen.c; kRunq: a runq v2 model for runq.c
     int hs = 0, kv_dim = 0, ctx = 0;
     int device = 0;
     bool pdl = true;
     cudaStream_t stream = nullptr;
     cudaGraphExec_t graph = nullptr;
-    uint8_t *image = nullptr;  // the whole .qwb on the device, same byte offsets as the file
+    uint8_t *image = nullptr;  // the weights on the device: the whole .qwb at its own offsets, or the runq arena
     size_t image_bytes = 0;
-    const float *attn_norm, *ffn_norm, *bq, *bk, *bv, *out_norm;
-    const int32_t *head_ids;
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr,
+                *out_norm = nullptr;
+    const int32_t *head_ids = nullptr;  // kQwen: token id of each head row; kRunq: none (row = token)
     std::vector<Mat> wq, wk, wv, wo, w1, w2, w3;
     Mat head, emb;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *hb = nullptr, *logits = nullptr, *kcache = nullptr,
@@ -176,21 +182,52 @@ static int decode_rt(int target, int n, int upt, bool pair) {
     return target < lim ? target : lim;
 }
 
-template <int BITS, int EPI, int PRO, int TAIL, int UPT>
+template <int BITS, int FAM, int EPI, int PRO, int TAIL, int UPT>
 static cudaError_t launch_decode(Model &m, DecodeParams p, int *count) {
     const size_t smem = decode_smem_bytes(p.n, p.rt, EPI, PRO, TAIL, p.d);
     p.counter = m.counters + *count;
     (*count)++;
-    return launch(decode_matvec_kernel<BITS, EPI, PRO, TAIL, UPT>, dim3((p.d + p.rt - 1) / p.rt), dim3(kThreads),
-                  smem, m.stream, m.pdl, p);
+    return launch(decode_matvec_kernel<BITS, FAM, EPI, PRO, TAIL, UPT>, dim3((p.d + p.rt - 1) / p.rt),
+                  dim3(kThreads), smem, m.stream, m.pdl, p);
+}
+
+// Head sizes the attention kernel is built for, per family (the loaders refuse others).
+template <int HS, int FAM>
+static cudaError_t set_attention_smem() {
+    // the attribute is per kernel, not per model: set it for the largest context any model may have, so that
+    // loading a model with a smaller context never lowers it under another model's launches
+    return cudaFuncSetAttribute(attention_kernel<HS, FAM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attention_smem_bytes<HS>(kMaxCtx));
+}
+
+static cudaError_t set_attention_smem_all() {
+    cudaError_t e;
+    if ((e = set_attention_smem<64, kQwen>()) != cudaSuccess || (e = set_attention_smem<32, kRunq>()) != cudaSuccess ||
+        (e = set_attention_smem<48, kRunq>()) != cudaSuccess || (e = set_attention_smem<64, kRunq>()) != cudaSuccess)
+        return e;
+    return cudaSuccess;
+}
+
+template <int FAM>
+static cudaError_t launch_attention(Model &m, const AttnParams &a) {
+    const dim3 grid(m.c.n_heads), block(kThreads);
+    const cudaStream_t s = m.stream;
+    switch (FAM == kQwen ? 64 : m.hs) {
+        case 32: return launch(attention_kernel<32, FAM>, grid, block, attention_smem_bytes<32>(m.ctx), s, m.pdl, a);
+        case 48: return launch(attention_kernel<48, FAM>, grid, block, attention_smem_bytes<48>(m.ctx), s, m.pdl, a);
+        default: return launch(attention_kernel<64, FAM>, grid, block, attention_smem_bytes<64>(m.ctx), s, m.pdl, a);
+    }
 }
 
 // Enqueues one forward step on m.stream (captured into a graph by the caller). With `ev`, records ev[k] before
 // kernel k and ev[count] after the last one; `info` receives each kernel's kind and layer; with `trace`, the
 // residual stream x is copied out after the embedding (slot 0) and after each layer's attention (2l + 1) and FFN
-// (2l + 2).
-static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
-                                std::vector<Model::Info> *info = nullptr, float *trace = nullptr) {
+// (2l + 2). The kernel sequence is the same for both families (qwen.c:490-573, runq.c:477-614); they differ in
+// the weight format (Q4 + fp16 scales vs Q8 + fp32 scales), the quantization rule, RoPE, biases and the head.
+template <int FAM>
+static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, std::vector<Model::Info> *info,
+                                       float *trace) {
+    constexpr int BITS = FAM == kQwen ? 4 : 8;  // layer matrices
     const Config &c = m.c;
     cudaError_t e;
     *count = 0;
@@ -206,7 +243,7 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
     };
     const int dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, L = c.n_layers;
     if ((e = mark("embed", -1)) != cudaSuccess) return e;
-    e = launch(embed_kernel, dim3((dim + kThreads - 1) / kThreads), dim3(kThreads), 0, m.stream, m.pdl,
+    e = launch(embed_kernel<FAM>, dim3((dim + kThreads - 1) / kThreads), dim3(kThreads), 0, m.stream, m.pdl,
                (const int8_t *)m.emb.w, m.emb.s, m.x, dim, m.st);
     (*count)++;
     if (e != cudaSuccess || (e = snap(0)) != cudaSuccess) return e;
@@ -219,20 +256,19 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
         p.n = dim; p.d = dim + 2 * kv; p.rt = decode_rt(8, dim, 1, false);
         p.src = m.x; p.norm_w = m.attn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.qkv; p.st = m.st;
         if ((e = mark("qkv", l)) != cudaSuccess ||
-            (e = launch_decode<4, kEpiStore, kProNorm, kTailNone, 1>(m, p, count)) != cudaSuccess)
+            (e = launch_decode<BITS, FAM, kEpiStore, kProNorm, kTailNone, 1>(m, p, count)) != cudaSuccess)
             return e;
         // attention
         AttnParams a = {};
         a.qkv = m.qkv;
-        a.bq = m.bq + (size_t)l * dim; a.bk = m.bk + (size_t)l * kv; a.bv = m.bv + (size_t)l * kv;
+        if (FAM == kQwen) {
+            a.bq = m.bq + (size_t)l * dim; a.bk = m.bk + (size_t)l * kv; a.bv = m.bv + (size_t)l * kv;
+        }
         a.rope = m.rope;
         a.kcache = m.kcache + (size_t)l * m.ctx * kv; a.vcache = m.vcache + (size_t)l * m.ctx * kv;
         a.xb = m.xb; a.dim = dim; a.kv_dim = kv; a.kv_mul = c.n_heads / c.n_kv_heads; a.ctx = m.ctx; a.st = m.st;
         a.et = m.et;
-        if ((e = mark("attention", l)) != cudaSuccess) return e;
-        if ((e = launch(attention_kernel<64>, dim3(c.n_heads), dim3(kThreads), attention_smem_bytes<64>(m.ctx),
-                        m.stream, m.pdl, a)) != cudaSuccess)
-            return e;
+        if ((e = mark("attention", l)) != cudaSuccess || (e = launch_attention<FAM>(m, a)) != cudaSuccess) return e;
         (*count)++;
         // o: quantize the attention output in every CTA, x += wo * it
         p = DecodeParams{};
@@ -240,7 +276,7 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
         p.n = dim; p.d = dim; p.rt = decode_rt(8, dim, 1, false);
         p.src = m.xb; p.out = m.x; p.st = m.st;
         if ((e = mark("o_proj", l)) != cudaSuccess ||
-            (e = launch_decode<4, kEpiResidual, kProQuant, kTailNone, 1>(m, p, count)) != cudaSuccess ||
+            (e = launch_decode<BITS, FAM, kEpiResidual, kProQuant, kTailNone, 1>(m, p, count)) != cudaSuccess ||
             (e = snap(2 * l + 1)) != cudaSuccess)
             return e;
         // gate/up: rmsnorm + quantize of x in every CTA, paired rows, SwiGLU -> hb
@@ -251,7 +287,7 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
         p.src = m.x; p.norm_w = m.ffn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.hb; p.st = m.st;
         p.et = m.et;
         if ((e = mark("gate_up", l)) != cudaSuccess ||
-            (e = launch_decode<4, kEpiSwiGLU, kProNorm, kTailNone, 4>(m, p, count)) != cudaSuccess)
+            (e = launch_decode<BITS, FAM, kEpiSwiGLU, kProNorm, kTailNone, 4>(m, p, count)) != cudaSuccess)
             return e;
         // down: quantize hb in every CTA, x += w2 * it; after the last layer, the last CTA normalizes x for the head
         p = DecodeParams{};
@@ -260,21 +296,27 @@ static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
         p.src = m.hb; p.out = m.x; p.st = m.st;
         p.tail_norm = m.out_norm; p.eps = c.rms_eps; p.tail_xq = m.xq_n; p.tail_xs = m.xs_n;
         if ((e = mark("down", l)) != cudaSuccess) return e;
-        e = l + 1 < L ? launch_decode<4, kEpiResidual, kProQuant, kTailNone, 5>(m, p, count)
-                      : launch_decode<4, kEpiResidual, kProQuant, kTailNormQuant, 5>(m, p, count);
+        e = l + 1 < L ? launch_decode<BITS, FAM, kEpiResidual, kProQuant, kTailNone, 5>(m, p, count)
+                      : launch_decode<BITS, FAM, kEpiResidual, kProQuant, kTailNormQuant, 5>(m, p, count);
         if (e != cudaSuccess || (e = snap(2 * l + 2)) != cudaSuccess) return e;
     }
-    // head: logits + argmax; the last CTA picks the next token
+    // head (qwen.c's trimmed Q8 head, or runq.c's classifier): logits + argmax; the last CTA picks the next token
     DecodeParams p = {};
     p.w[0] = m.head.w; p.ws[0] = m.head.s; p.rows[0] = c.head_k;
     p.n = dim; p.d = c.head_k; p.rt = decode_rt(32, dim, 4, false);
     p.xq = m.xq_n; p.xs = m.xs_n; p.out = m.logits; p.st = m.st;
     p.prompt = m.prompt; p.head_ids = m.head_ids; p.ids = m.ids; p.cap = m.ctx;
     if ((e = mark("head", -1)) != cudaSuccess ||
-        (e = launch_decode<8, kEpiHead, kProQuantized, kTailNextToken, 4>(m, p, count)) != cudaSuccess)
+        (e = launch_decode<8, FAM, kEpiHead, kProQuantized, kTailNextToken, 4>(m, p, count)) != cudaSuccess)
         return e;
     if (ev) e = cudaEventRecordWithFlags(ev[*count], m.stream, cudaEventRecordExternal);
     return e;
+}
+
+static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
+                                std::vector<Model::Info> *info = nullptr, float *trace = nullptr) {
+    return m.family == kRunq ? enqueue_step_family<kRunq>(m, count, ev, info, trace)
+                             : enqueue_step_family<kQwen>(m, count, ev, info, trace);
 }
 
 // Algorithmic bytes of kernel k of the step at position `pos`: every byte the kernel must move at least once
@@ -283,19 +325,22 @@ static double kernel_bytes(const Model &m, int k, int pos) {
     const Config &c = m.c;
     const double dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, ng = dim / 32;
     const char *kind = m.info[k].kind;
-    auto q4 = [](double d, double n) { return d * n / 2 + d * (n / 32) * 2; };
-    if (!strcmp(kind, "embed")) return dim + ng * 2 + dim * 4;
+    const bool runq = m.family == kRunq;
+    const double sb = runq ? 4 : 2;  // bytes per weight scale
+    // one layer matrix: Q4 + fp16 scales (qwen.c) or Q8 + fp32 scales (runq.c)
+    auto mat = [&](double d, double n) { return d * n * (runq ? 1.0 : 0.5) + d * (n / 32) * sb; };
+    if (!strcmp(kind, "embed")) return dim + ng * sb + dim * 4;
     // matvecs: weights + scales, int8 input + scales, outputs (read + write for residual updates); tails: the
     // vector they normalize or quantize, the norm weight, the int8 output
     const bool last = m.info[k].layer == c.n_layers - 1;
-    if (!strcmp(kind, "qkv")) return q4(dim + 2 * kv, dim) + dim * 4 * 2 + (dim + 2 * kv) * 4;
-    if (!strcmp(kind, "attention"))
-        return (dim + 2 * kv) * 4 * 2 + m.hs * 4 + 2.0 * pos * kv * 4 + 2 * kv * 4 + dim * 4;
-    if (!strcmp(kind, "o_proj")) return q4(dim, dim) + dim * 4 + dim * 8;
-    if (!strcmp(kind, "gate_up")) return 2 * q4(hid, dim) + dim * 4 * 2 + hid * 4;
-    if (!strcmp(kind, "down")) return q4(dim, hid) + hid * 4 + dim * 8 + (last ? dim * 4 * 2 + dim + ng * 4 : 0);
+    if (!strcmp(kind, "qkv")) return mat(dim + 2 * kv, dim) + dim * 4 * 2 + (dim + 2 * kv) * 4;
+    if (!strcmp(kind, "attention"))  // q/k/v in (+ biases), RoPE row, cached rows read, this row written, output
+        return (dim + 2 * kv) * 4 * (runq ? 1 : 2) + m.hs * 4 + 2.0 * pos * kv * 4 + 2 * kv * 4 + dim * 4;
+    if (!strcmp(kind, "o_proj")) return mat(dim, dim) + dim * 4 + dim * 8;
+    if (!strcmp(kind, "gate_up")) return 2 * mat(hid, dim) + dim * 4 * 2 + hid * 4;
+    if (!strcmp(kind, "down")) return mat(dim, hid) + hid * 4 + dim * 8 + (last ? dim * 4 * 2 + dim + ng * 4 : 0);
     if (!strcmp(kind, "head"))
-        return (double)c.head_k * dim + (double)c.head_k * ng * 2 + dim + ng * 4 + c.head_k * 4.0;
+        return (double)c.head_k * dim + (double)c.head_k * ng * sb + dim + ng * 4 + c.head_k * 4.0;
     return 16;
 }
 
@@ -381,7 +426,7 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
     auto gemm = [&](const Mat &w, int n, int d, float *out, int ldo) {
         return gemm_launch(w.w, w.s, b.xq, b.xs, out, n, d, count, ldx, ldo, 4, s);
     };
-    embed_rows_kernel<<<count, T, 0, s>>>((const int8_t *)m.emb.w, m.emb.s, tokens, b.x, dim);
+    embed_rows_kernel<<<count, T, 0, s>>>((const int8_t *)m.emb.w, (const uint16_t *)m.emb.s, tokens, b.x, dim);
     for (int l = 0; l < L; l++) {
         norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, m.attn_norm + (size_t)l * dim, c.rms_eps, dim, b.xq,
                                                              b.xs, ldx);
@@ -415,11 +460,120 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
     return 0;
 }
 
-}  // namespace qwen
+}  // namespace decode
 }  // namespace mvb
 
 using namespace mvb;
-using namespace mvb::qwen;
+using namespace mvb::decode;
+
+namespace mvb {
+namespace decode {
+
+// The second half of loading, common to both families: with the config, the weight pointers and the RoPE table
+// (ctx * hs floats) in place, allocates the activations, caches and state, and captures the step graphs.
+// Returns m, or null after set_error() (m is freed).
+static Model *finish_load(Model *m, const std::vector<float> &rope, const char *who) {
+    const Config &c = m->c;
+    const int dim = c.dim, kv = m->kv_dim, hid = c.hidden_dim, L = c.n_layers;
+    cudaError_t e = cudaSuccess;
+    auto fail = [&](const char *what) -> Model * {
+        set_error("%s: %s: %s", who, what, cudaGetErrorString(e));
+        destroy(m);
+        return nullptr;
+    };
+    const size_t kvbytes = (size_t)L * m->ctx * kv * 4;
+    if ((e = cudaMalloc(&m->x, dim * 4)) != cudaSuccess || (e = cudaMalloc(&m->xb, dim * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->qkv, (dim + 2 * kv) * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->hb, (size_t)hid * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->logits, (size_t)c.head_k * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->kcache, kvbytes)) != cudaSuccess || (e = cudaMalloc(&m->vcache, kvbytes)) != cudaSuccess ||
+        (e = cudaMalloc(&m->rope, rope.size() * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->xq_n, dim)) != cudaSuccess || (e = cudaMalloc(&m->xs_n, dim / 32 * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->counters, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->prompt, (size_t)m->ctx * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->ids, (size_t)m->ctx * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->st, sizeof(State))) != cudaSuccess)
+        return fail("buffers");
+    if ((e = cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemset(m->kcache, 0, kvbytes)) != cudaSuccess ||
+        (e = cudaMemset(m->vcache, 0, kvbytes)) != cudaSuccess ||
+        (e = cudaMemset(m->st, 0, sizeof(State))) != cudaSuccess ||
+        (e = cudaMemset(m->counters, 0, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
+        (e = set_attention_smem_all()) != cudaSuccess)
+        return fail("init");
+    if ((e = cudaHostAlloc(&m->ring, sizeof(State) * Model::kRing, cudaHostAllocDefault)) != cudaSuccess)
+        return fail("pinned state");
+    m->et = expf_table_device();
+    if (!m->et.slots) {
+        e = cudaErrorUnknown;
+        return fail("expf table");
+    }
+    // capture one forward step, then the instrumented copy (events between kernels, no programmatic overlap)
+    for (int pass = 0; pass < 2; pass++) {
+        cudaGraph_t graph;
+        int count = 0;
+        const bool pdl = m->pdl;
+        if (pass == 1) {
+            m->pdl = false;
+            m->prof_ev.resize(m->kernels_per_step + 1);
+            for (auto &ev : m->prof_ev)
+                if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail("events");
+        }
+        if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+            return fail("capture");
+        cudaError_t le = pass == 0 ? enqueue_step(*m, &count, nullptr, &m->info)
+                                   : enqueue_step(*m, &count, m->prof_ev.data(), nullptr);
+        e = cudaStreamEndCapture(m->stream, &graph);
+        m->pdl = pdl;
+        if (le != cudaSuccess) {
+            e = le;
+            return fail("kernel launch");
+        }
+        if (e != cudaSuccess) return fail("capture");
+        e = cudaGraphInstantiate(pass == 0 ? &m->graph : &m->prof_graph, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail("graph");
+        if (pass == 0) m->kernels_per_step = count;
+    }
+    return m;
+}
+
+// Device, stream and PDL setting of a new model. 0, or -1 after set_error().
+static int open_device(Model *m, const char *who) {
+    cudaError_t e = cudaGetDevice(&m->device);
+    if (const char *pd = getenv("MVB_PDL")) m->pdl = atoi(pd) != 0;
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        set_error("%s: %s", who, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+// Maps a whole file read-only (for the file loaders: the weights go from the page cache straight to HBM).
+struct FileMap {
+    void *p = nullptr;
+    size_t n = 0;
+    explicit FileMap(const char *path) {
+        const int fd = path ? open(path, O_RDONLY) : -1;
+        if (fd < 0) return;
+        struct stat st;
+        if (fstat(fd, &st) == 0 && st.st_size > 0) {
+            void *q = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+            if (q != MAP_FAILED) {
+                p = q;
+                n = (size_t)st.st_size;
+            }
+        }
+        close(fd);
+    }
+    ~FileMap() {
+        if (p) munmap(p, n);
+    }
+};
+
+}  // namespace decode
+}  // namespace mvb
 
 extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
     clear_error();
@@ -435,6 +589,7 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
         return nullptr;
     }
     Model *m = new Model;
+    m->family = kQwen;
     memcpy(&m->c, b + 8, sizeof(Config));
     Config &c = m->c;
     // qwen.c:223-228's checks, plus this implementation's own limits
@@ -487,28 +642,28 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
             delete m;
             return nullptr;
         }
-    cudaError_t e = cudaGetDevice(&m->device);
-    if (const char *pd = getenv("MVB_PDL")) m->pdl = atoi(pd) != 0;
-    auto fail = [&](const char *what) -> void * {
-        set_error("mvb_qwen_load: %s: %s", what, cudaGetErrorString(e));
+    if (open_device(m, "mvb_qwen_load")) {
         destroy(m);
         return nullptr;
-    };
-    if (e != cudaSuccess) return fail("no device");
-    if ((e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking)) != cudaSuccess) return fail("stream");
-    if ((e = cudaMalloc(&m->image, bytes)) != cudaSuccess) return fail("weights");
-    if ((e = cudaMemcpy(m->image, image, bytes, cudaMemcpyHostToDevice)) != cudaSuccess) return fail("upload");
+    }
+    cudaError_t e;
+    if ((e = cudaMalloc(&m->image, bytes)) != cudaSuccess ||
+        (e = cudaMemcpy(m->image, image, bytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
+        set_error("mvb_qwen_load: weights: %s", cudaGetErrorString(e));
+        destroy(m);
+        return nullptr;
+    }
     m->image_bytes = bytes;
     auto at = [&](size_t o) { return m->image + o; };
     m->attn_norm = (const float *)at(o_attn); m->ffn_norm = (const float *)at(o_ffn);
     m->bq = (const float *)at(o_bq); m->bk = (const float *)at(o_bk); m->bv = (const float *)at(o_bv);
     m->out_norm = (const float *)at(o_norm); m->head_ids = (const int32_t *)at(o_ids);
     auto conv = [&](const std::vector<MatOff> &v, std::vector<Mat> &dst) {
-        for (auto &x : v) dst.push_back(Mat{at(x.w), (const uint16_t *)at(x.s)});
+        for (auto &x : v) dst.push_back(Mat{at(x.w), at(x.s)});
     };
     conv(q, m->wq); conv(k, m->wk); conv(vv, m->wv); conv(o, m->wo); conv(g, m->w1); conv(dn, m->w2); conv(u, m->w3);
-    m->head = Mat{at(hd[0].w), (const uint16_t *)at(hd[0].s)};
-    m->emb = Mat{at(em[0].w), (const uint16_t *)at(em[0].s)};
+    m->head = Mat{at(hd[0].w), at(hd[0].s)};
+    m->emb = Mat{at(em[0].w), at(em[0].s)};
     // RoPE table, exactly qwen.c:504-508 per position
     std::vector<float> rope((size_t)m->ctx * m->hs);
     for (int pos = 0; pos < m->ctx; pos++)
@@ -517,63 +672,146 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
             rope[(size_t)pos * m->hs + i] = (float)cos(a);
             rope[(size_t)pos * m->hs + m->hs / 2 + i] = (float)sin(a);
         }
-    const size_t kvbytes = (size_t)L * m->ctx * kv * 4;
-    if ((e = cudaMalloc(&m->x, dim * 4)) != cudaSuccess || (e = cudaMalloc(&m->xb, dim * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->qkv, (dim + 2 * kv) * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->hb, (size_t)hid * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->logits, (size_t)c.head_k * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->kcache, kvbytes)) != cudaSuccess || (e = cudaMalloc(&m->vcache, kvbytes)) != cudaSuccess ||
-        (e = cudaMalloc(&m->rope, rope.size() * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->xq_n, dim)) != cudaSuccess || (e = cudaMalloc(&m->xs_n, dim / 32 * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->counters, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->prompt, (size_t)m->ctx * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->ids, (size_t)m->ctx * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->st, sizeof(State))) != cudaSuccess)
-        return fail("buffers");
-    if ((e = cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
-        (e = cudaMemset(m->kcache, 0, kvbytes)) != cudaSuccess || (e = cudaMemset(m->vcache, 0, kvbytes)) != cudaSuccess ||
-        (e = cudaMemset(m->st, 0, sizeof(State))) != cudaSuccess ||
-        (e = cudaMemset(m->counters, 0, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
-        // the attribute is per kernel, not per model: set it for the largest context any model may have, so that
-        // loading a model with a smaller context never lowers it under another model's launches
-        (e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)attention_smem_bytes<64>(kMaxCtx))) != cudaSuccess)
-        return fail("init");
-    if ((e = cudaHostAlloc(&m->ring, sizeof(State) * Model::kRing, cudaHostAllocDefault)) != cudaSuccess)
-        return fail("pinned state");
-    m->et = expf_table_device();
-    if (!m->et.slots) {
-        e = cudaErrorUnknown;
-        return fail("expf table");
+    return finish_load(m, rope, "mvb_qwen_load");
+}
+
+extern "C" void *mvb_qwen_load_file(const char *path, int ctx) {
+    clear_error();
+    FileMap f(path);
+    if (!f.p) {
+        set_error("mvb_qwen_load_file: cannot map %s", path ? path : "(null)");
+        return nullptr;
     }
-    // capture one forward step, then the instrumented copy (events between kernels, no programmatic overlap)
-    for (int pass = 0; pass < 2; pass++) {
-        cudaGraph_t graph;
-        int count = 0;
-        const bool pdl = m->pdl;
-        if (pass == 1) {
-            m->pdl = false;
-            m->prof_ev.resize(m->kernels_per_step + 1);
-            for (auto &ev : m->prof_ev)
-                if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail("events");
-        }
-        if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
-            return fail("capture");
-        cudaError_t le = pass == 0 ? enqueue_step(*m, &count, nullptr, &m->info)
-                                   : enqueue_step(*m, &count, m->prof_ev.data(), nullptr);
-        e = cudaStreamEndCapture(m->stream, &graph);
-        m->pdl = pdl;
-        if (le != cudaSuccess) {
-            e = le;
-            return fail("kernel launch");
-        }
-        if (e != cudaSuccess) return fail("capture");
-        e = cudaGraphInstantiate(pass == 0 ? &m->graph : &m->prof_graph, graph, 0);
-        cudaGraphDestroy(graph);
-        if (e != cudaSuccess) return fail("graph");
-        if (pass == 0) m->kernels_per_step = count;
+    return mvb_qwen_load(f.p, f.n, ctx);
+}
+
+// runq v2 checkpoint (runq.c:318-357): 256-byte header, fp32 rmsnorm weights, then int8 values each followed by
+// their fp32 group scales (runq.c:274-289) for the embedding, wq, wk, wv, wo, w1, w2, w3 (per layer) and, unless it
+// is shared with the embedding, the classifier (runq.c:291-316). The file's tensors follow one another with no
+// padding; here each is copied into its own 256-byte-aligned slot of one device allocation (the kernels read
+// weights 16 bytes at a time), straight from the caller's bytes: no host copy is made.
+extern "C" void *mvb_runq_load(const void *image, size_t bytes, int ctx) {
+    clear_error();
+    const uint8_t *b = static_cast<const uint8_t *>(image);
+    uint32_t magic = 0;
+    int32_t version = 0;
+    if (b && bytes >= 256) {
+        memcpy(&magic, b, 4);
+        memcpy(&version, b + 4, 4);
     }
-    return m;
+    if (!b || bytes < 256 || magic != 0x616b3432 || version != 2) {  // runq.c:322-329
+        set_error("mvb_runq_load: not a runq version 2 checkpoint");
+        return nullptr;
+    }
+    int32_t h[7];  // dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len (runq.c:28-36)
+    memcpy(h, b + 8, sizeof h);
+    const uint8_t shared = b[36];
+    int32_t gs;
+    memcpy(&gs, b + 37, 4);
+    Model *m = new Model;
+    m->family = kRunq;
+    Config &c = m->c;
+    c = Config{};
+    c.dim = h[0]; c.hidden_dim = h[1]; c.n_layers = h[2]; c.n_heads = h[3]; c.n_kv_heads = h[4];
+    c.vocab_size = h[5]; c.max_seq_len = h[6]; c.group_size = gs; c.emb_bits = 8;
+    c.head_k = c.vocab_size;  // the classifier has a row per token
+    c.rope_theta = 10000.0f;  // runq.c:508
+    c.rms_eps = 1e-5f;        // runq.c:401
+    const int hs = c.n_heads > 0 ? c.dim / c.n_heads : 0;
+    // runq.c accepts group size 32 or 64 (runq.c:335-337); this decode is built for 32 (64 runs through
+    // fpga_matvec); head sizes 32, 48 (stories15M) and 64 (stories110M)
+    if (gs != 32 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.dim % c.n_heads || c.n_heads % c.n_kv_heads ||
+        (hs != 32 && hs != 48 && hs != 64) || c.dim % 32 || c.hidden_dim % 32 || c.dim > kMaxDim ||
+        c.hidden_dim > kMaxN || c.vocab_size <= 0 || c.n_layers <= 0 || c.max_seq_len <= 0) {
+        set_error("mvb_runq_load: unsupported config (group %d, dim %d, hidden %d, heads %d/%d; this decode needs "
+                  "group size 32, head size 32, 48 or 64, dim <= %d, hidden <= %d)", gs, c.dim, c.hidden_dim,
+                  c.n_heads, c.n_kv_heads, kMaxDim, kMaxN);
+        delete m;
+        return nullptr;
+    }
+    m->hs = hs;
+    m->kv_dim = hs * c.n_kv_heads;
+    m->ctx = ctx < c.max_seq_len ? ctx : c.max_seq_len;
+    if (m->ctx < 2 || m->ctx > kMaxCtx) {
+        set_error("mvb_runq_load: context %d outside [2, %d]", m->ctx, kMaxCtx);
+        delete m;
+        return nullptr;
+    }
+    // the file's tensors in order (source offset, bytes) and their slots in the device arena
+    const int L = c.n_layers, dim = c.dim, kv = m->kv_dim, hid = c.hidden_dim;
+    struct Piece { size_t src, bytes, dst; };
+    std::vector<Piece> pieces;
+    size_t src = 256, dst = 0;
+    auto piece = [&](size_t n) {
+        pieces.push_back(Piece{src, n, dst});
+        src += n;
+        dst += (n + 255) & ~(size_t)255;
+        return pieces.size() - 1;
+    };
+    const size_t p_att = piece((size_t)L * dim * 4), p_ffn = piece((size_t)L * dim * 4), p_fin = piece((size_t)dim * 4);
+    struct MatPiece { size_t q, s; };
+    auto mats = [&](int count, size_t d, size_t n) {
+        std::vector<MatPiece> v(count);
+        for (auto &x : v) {
+            x.q = piece(d * n);
+            x.s = piece(d * n / 32 * 4);
+        }
+        return v;
+    };
+    auto em = mats(1, c.vocab_size, dim);
+    auto q = mats(L, dim, dim), k = mats(L, kv, dim), vv = mats(L, kv, dim), o = mats(L, dim, dim),
+         w1 = mats(L, hid, dim), w2 = mats(L, dim, hid), w3 = mats(L, hid, dim);
+    auto cls = shared ? em : mats(1, c.vocab_size, dim);
+    if (src > bytes) {
+        set_error("mvb_runq_load: checkpoint is %zu bytes, but its header describes %zu", bytes, src);
+        delete m;
+        return nullptr;
+    }
+    if (open_device(m, "mvb_runq_load")) {
+        destroy(m);
+        return nullptr;
+    }
+    cudaError_t e = cudaMalloc(&m->image, dst);
+    for (size_t i = 0; e == cudaSuccess && i < pieces.size(); i++)
+        e = cudaMemcpy(m->image + pieces[i].dst, b + pieces[i].src, pieces[i].bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        set_error("mvb_runq_load: weights: %s", cudaGetErrorString(e));
+        destroy(m);
+        return nullptr;
+    }
+    m->image_bytes = dst;
+    auto at = [&](size_t i) { return m->image + pieces[i].dst; };
+    m->attn_norm = (const float *)at(p_att);
+    m->ffn_norm = (const float *)at(p_ffn);
+    m->out_norm = (const float *)at(p_fin);
+    auto conv = [&](const std::vector<MatPiece> &v, std::vector<Mat> &out) {
+        for (auto &x : v) out.push_back(Mat{at(x.q), at(x.s)});
+    };
+    conv(q, m->wq); conv(k, m->wk); conv(vv, m->wv); conv(o, m->wo); conv(w1, m->w1); conv(w2, m->w2); conv(w3, m->w3);
+    m->emb = Mat{at(em[0].q), at(em[0].s)};
+    m->head = Mat{at(cls[0].q), at(cls[0].s)};
+    // RoPE table per position, computed as runq.c:506-512 does it (float powf/cosf/sinf of the host C library);
+    // pair j of a head is (2j, 2j + 1), whose head_dim is 2j
+    std::vector<float> rope((size_t)m->ctx * hs);
+    for (int pos = 0; pos < m->ctx; pos++)
+        for (int j = 0; j < hs / 2; j++) {
+            const int head_dim = 2 * j;
+            const float freq = 1.0f / powf(10000.0f, head_dim / (float)hs);
+            const float val = pos * freq;
+            rope[(size_t)pos * hs + j] = cosf(val);
+            rope[(size_t)pos * hs + hs / 2 + j] = sinf(val);
+        }
+    return finish_load(m, rope, "mvb_runq_load");
+}
+
+extern "C" void *mvb_runq_load_file(const char *path, int ctx) {
+    clear_error();
+    FileMap f(path);
+    if (!f.p) {
+        set_error("mvb_runq_load_file: cannot map %s", path ? path : "(null)");
+        return nullptr;
+    }
+    return mvb_runq_load(f.p, f.n, ctx);
 }
 
 extern "C" void mvb_qwen_free(void *model) { destroy(static_cast<Model *>(model)); }
@@ -656,11 +894,21 @@ static int check_prompt(Model *m, const int *prompt, int n, const char *who) {
     return 0;
 }
 
+// The same state reached one decode step per fed token (the reference's own order of work).
+extern "C" int mvb_qwen_prefill_tokenwise(void *model, const int *prompt, int n) {
+    Model *m = static_cast<Model *>(model);
+    if (check_prompt(m, prompt, n, "mvb_qwen_prefill_tokenwise")) return -1;
+    if (set_state(*m, prompt[0], 0, n) || mvb_qwen_launch(m, n - 1)) return -1;
+    return wait_stream(*m, "mvb_qwen_prefill_tokenwise", timeout_s() + 0.01 * n);
+}
+
 // Feeds prompt[0 .. n-2] (positions 0 .. n-2), leaving prompt[n-1] as the token of position n-1: the state
-// qwen.c's generate() is in just before its first sampled token. The fed tokens go through the layers in batches
-// (tensor-core matmuls), writing the same KV-cache rows one decode step per token would.
+// qwen.c's (and runq.c's) generate() is in just before its first sampled token. For a .qwb model the fed tokens go
+// through the layers in batches (tensor-core matmuls), writing the same KV-cache rows one decode step per token
+// would; a runq model takes one decode step per token.
 extern "C" int mvb_qwen_prefill(void *model, const int *prompt, int n) {
     Model *m = static_cast<Model *>(model);
+    if (m && m->family == kRunq) return mvb_qwen_prefill_tokenwise(model, prompt, n);
     if (check_prompt(m, prompt, n, "mvb_qwen_prefill")) return -1;
     for (int p0 = 0; p0 < n - 1; p0 += kBatchCap)
         if (prefill_batch(*m, m->prompt + p0, p0, (n - 1 - p0) < kBatchCap ? n - 1 - p0 : kBatchCap)) return -1;
@@ -672,14 +920,6 @@ extern "C" int mvb_qwen_prefill(void *model, const int *prompt, int n) {
         return -1;
     }
     return 0;
-}
-
-// The same state reached one decode step per fed token (the reference's own order of work).
-extern "C" int mvb_qwen_prefill_tokenwise(void *model, const int *prompt, int n) {
-    Model *m = static_cast<Model *>(model);
-    if (check_prompt(m, prompt, n, "mvb_qwen_prefill_tokenwise")) return -1;
-    if (set_state(*m, prompt[0], 0, n) || mvb_qwen_launch(m, n - 1)) return -1;
-    return wait_stream(*m, "mvb_qwen_prefill_tokenwise", timeout_s() + 0.01 * n);
 }
 
 // Copies the KV cache rows of positions 0 .. positions-1 of every layer to k and v (host, n_layers * positions *
@@ -806,8 +1046,10 @@ extern "C" int mvb_qwen_kernel_info(void *model, int k, int pos, char *kind, int
     return 0;
 }
 
-// qwen.c generate() at temperature 0 (qwen.c:669-712): prompt fed one position at a time, then greedy tokens
-// until `steps` are generated, <|im_end|>/<|endoftext|> is sampled, or the context is full. Returns the count.
+// qwen.c generate() at temperature 0 (qwen.c:669-712) for a .qwb model, runq.c generate() at temperature 0
+// (runq.c:982-1026) for a runq model: the prompt fed (mvb_qwen_prefill), then greedy tokens until `steps` are
+// generated, a stop token is sampled (<|im_end|> or <|endoftext|> for qwen.c, BOS = 1 for runq.c, runq.c:1016), or
+// the context is full. Returns the count, stop token excluded.
 extern "C" int mvb_qwen_generate(void *model, const int *prompt, int n_prompt, int steps, int *ids) {
     Model *m = static_cast<Model *>(model);
     if (!m || !ids || steps < 1) {
@@ -819,8 +1061,12 @@ extern "C" int mvb_qwen_generate(void *model, const int *prompt, int n_prompt, i
     const int n = steps < room ? steps : room;
     if (mvb_qwen_decode(model, n, ids) != n) return -1;
     for (int i = 0; i < n; i++)
-        if (ids[i] == kImEnd || ids[i] == kEndOfText) return i;
+        if (m->family == kRunq ? ids[i] == 1 : (ids[i] == kImEnd || ids[i] == kEndOfText)) return i;
     return n;
+}
+
+extern "C" int mvb_runq_generate(void *model, const int *prompt, int n_prompt, int steps, int *ids) {
+    return mvb_qwen_generate(model, prompt, n_prompt, steps, ids);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -828,7 +1074,7 @@ extern "C" int mvb_qwen_generate(void *model, const int *prompt, int n_prompt, i
 // scratch that lives in a file-scope device array, then the head matvec reading it. For callers that cannot
 // allocate device memory (see mvb_norm_matvec4_static in include/matvec_b200.h).
 namespace mvb {
-namespace qwen {
+namespace decode {
 
 constexpr int kStaticNormMatvecMaxN = kMaxDim;  // 2048 columns
 // n int8 quantized activations at offset 0, their n/32 fp32 scales at offset kStaticNormMatvecMaxN
@@ -854,12 +1100,12 @@ static uint8_t *scratch_address(int dev) {
     return static_cast<uint8_t *>(p);
 }
 
-}  // namespace qwen
+}  // namespace decode
 }  // namespace mvb
 
 extern "C" int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, const void *w, const void *ws,
                                        float *out, int n, int d, int wbits, void *stream) {
-    using namespace mvb::qwen;
+    using namespace mvb::decode;
     if (!x || !norm_w) {
         set_error("mvb_norm_matvec4_static: null pointer argument");
         return -1;
