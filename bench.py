@@ -490,6 +490,8 @@ def step_mode(args):
     mvb = load_pkg()
     torch.cuda.set_device(0)
     dec = mvb.QwenDecoder(model_path(0, 1), ctx=512)
+    if args.full_head:
+        dec.full_head(True)
     stream = torch.cuda.ExternalStream(dec.stream_handle)
     prompt = prompt_ids()
     dec.prefill(prompt)
@@ -504,8 +506,9 @@ def step_mode(args):
         ts.append(e0.elapsed_time(e1))
     dec.close()
     ms = statistics.median(ts)
-    print(json.dumps({"mode": "step", "ms_per_token": round(ms, 4), "tok_s": round(1000 / ms, 1),
-                      "steps": args.steps, "warmup": args.warmup}))
+    print(json.dumps({"mode": "step", "head": "full vocabulary" if args.full_head else "trimmed (head_ids)",
+                      "ms_per_token": round(ms, 4), "tok_s": round(1000 / ms, 1), "steps": args.steps,
+                      "warmup": args.warmup}))
 
 
 def sharded_mode(args, rank, world, local_rank):
@@ -782,6 +785,7 @@ def main():
     ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
     ap.add_argument("--model", default="", choices=["", *RUNQ_MODELS], help="runq: only this model")
+    ap.add_argument("--full-head", action="store_true", help="step: the full-vocabulary head (mvb_qwen_full_head)")
     ap.add_argument("--mode", default="decode",
                     choices=["decode", "sweep", "sharded", "prefill", "prompt", "step", "runq"],
                     help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "

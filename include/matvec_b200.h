@@ -71,8 +71,16 @@ void *mvb_runq_load(const void *checkpoint, size_t bytes, int ctx);
 /* mvb_runq_load of the checkpoint file at `path`, mapped read-only (no host copy). */
 void *mvb_runq_load_file(const char *path, int ctx);
 
-/* out[0..8] = dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, head_k, ctx, kernels per step. */
+/* out[0..8] = dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, head rows in use (head_k, or
+ * vocab_size with a full head), ctx, kernels per step. */
 int mvb_qwen_config(void *model, int *out);
+
+/* on = 1: the head of a .qwb model becomes the full vocabulary. Qwen2 ties its output head to the token embedding,
+ * so the Q8 embedding (vocab_size rows) serves as the head and its argmax row is the token id; on = 0: back to
+ * the file's trimmed head_k-row head mapped through head_ids (qwen.c's). The trimmed head's logit i equals the
+ * full head's logit head_ids[i] bit for bit. Recaptures the step; the KV cache and state are kept. A runq
+ * handle's classifier is already full (on = 1 returns 0). No counterpart in the reference. 0, or -1. */
+int mvb_qwen_full_head(void *model, int on);
 
 /* The model's CUDA stream (every launch of the model is on it). */
 void *mvb_qwen_stream(void *model);

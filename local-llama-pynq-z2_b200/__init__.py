@@ -83,6 +83,8 @@ def lib():
         for name in ("mvb_qwen_generate", "mvb_runq_generate"):
             getattr(L, name).restype = i
             getattr(L, name).argtypes = [vp, ip, i, i, ip]
+        L.mvb_qwen_full_head.restype = i
+        L.mvb_qwen_full_head.argtypes = [vp, i]
         L.mvb_qwen_rewind.restype = i
         L.mvb_qwen_rewind.argtypes = [vp, i, i, i]
         L.mvb_qwen_launch.restype = i
@@ -353,8 +355,11 @@ class QwenDecoder:
         if not h:
             raise MatvecError(who + " failed: " + last_error())
         self.h = h
+        self._read_config()
+
+    def _read_config(self):
         cfg = (C.c_int * 9)()
-        lib().mvb_qwen_config(h, cfg)
+        check(lib().mvb_qwen_config(self.h, cfg), "mvb_qwen_config")
         keys = ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size", "head_k", "ctx",
                 "kernels_per_step")
         self.cfg = dict(zip(keys, list(cfg)))
@@ -409,6 +414,11 @@ class QwenDecoder:
         if n < 0:
             raise MatvecError("mvb_qwen_generate failed: " + last_error())
         return out[:n]
+
+    def full_head(self, on=True):
+        """Use the whole vocabulary (the tied Q8 embedding) as the head instead of the trimmed head_ids head."""
+        check(lib().mvb_qwen_full_head(self.h, int(bool(on))), "mvb_qwen_full_head")
+        self._read_config()
 
     def rewind(self, token, pos, n_prompt):
         check(lib().mvb_qwen_rewind(self.h, token, pos, n_prompt), "mvb_qwen_rewind")

@@ -120,6 +120,9 @@ struct Model {
     const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr,
                 *out_norm = nullptr;
     const int32_t *head_ids = nullptr;  // kQwen: token id of each head row; kRunq: none (row = token)
+    int head_rows = 0;                  // rows of the head in use: head_k, or vocab_size for a full head
+    Mat head_trim = {};                 // the file's head and its ids, kept while a full head is in use
+    const int32_t *ids_trim = nullptr;
     std::vector<Mat> wq, wk, wv, wo, w1, w2, w3;
     Mat head, emb;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *hb = nullptr, *logits = nullptr, *kcache = nullptr,
@@ -302,8 +305,8 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
     }
     // head (qwen.c's trimmed Q8 head, or runq.c's classifier): logits + argmax; the last CTA picks the next token
     DecodeParams p = {};
-    p.w[0] = m.head.w; p.ws[0] = m.head.s; p.rows[0] = c.head_k;
-    p.n = dim; p.d = c.head_k; p.rt = decode_rt(32, dim, 4, false);
+    p.w[0] = m.head.w; p.ws[0] = m.head.s; p.rows[0] = m.head_rows;
+    p.n = dim; p.d = m.head_rows; p.rt = decode_rt(32, dim, 4, false);
     p.xq = m.xq_n; p.xs = m.xs_n; p.out = m.logits; p.st = m.st;
     p.prompt = m.prompt; p.head_ids = m.head_ids; p.ids = m.ids; p.cap = m.ctx;
     if ((e = mark("head", -1)) != cudaSuccess ||
@@ -340,7 +343,7 @@ static double kernel_bytes(const Model &m, int k, int pos) {
     if (!strcmp(kind, "gate_up")) return 2 * mat(hid, dim) + dim * 4 * 2 + hid * 4;
     if (!strcmp(kind, "down")) return mat(dim, hid) + hid * 4 + dim * 8 + (last ? dim * 4 * 2 + dim + ng * 4 : 0);
     if (!strcmp(kind, "head"))
-        return (double)c.head_k * dim + (double)c.head_k * ng * sb + dim + ng * 4 + c.head_k * 4.0;
+        return (double)m.head_rows * dim + (double)m.head_rows * ng * sb + dim + ng * 4 + m.head_rows * 4.0;
     return 16;
 }
 
@@ -469,6 +472,41 @@ using namespace mvb::decode;
 namespace mvb {
 namespace decode {
 
+// Captures one forward step into m->graph, then the instrumented copy (events between kernels, no programmatic
+// overlap) into m->prof_graph, replacing any earlier capture. Nothing of the model may be in flight.
+static cudaError_t capture_graphs(Model *m) {
+    cudaError_t e;
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->prof_graph) cudaGraphExecDestroy(m->prof_graph);
+    m->graph = m->prof_graph = nullptr;
+    for (cudaEvent_t ev : m->prof_ev) cudaEventDestroy(ev);
+    m->prof_ev.clear();
+    m->info.clear();
+    for (int pass = 0; pass < 2; pass++) {
+        cudaGraph_t graph;
+        int count = 0;
+        const bool pdl = m->pdl;
+        if (pass == 1) {
+            m->pdl = false;
+            m->prof_ev.resize(m->kernels_per_step + 1);
+            for (auto &ev : m->prof_ev)
+                if ((e = cudaEventCreate(&ev)) != cudaSuccess) return e;
+        }
+        if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess) return e;
+        cudaError_t le = pass == 0 ? enqueue_step(*m, &count, nullptr, &m->info)
+                                   : enqueue_step(*m, &count, m->prof_ev.data(), nullptr);
+        e = cudaStreamEndCapture(m->stream, &graph);
+        m->pdl = pdl;
+        if (le != cudaSuccess) return le;
+        if (e != cudaSuccess) return e;
+        e = cudaGraphInstantiate(pass == 0 ? &m->graph : &m->prof_graph, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return e;
+        if (pass == 0) m->kernels_per_step = count;
+    }
+    return cudaSuccess;
+}
+
 // The second half of loading, common to both families: with the config, the weight pointers and the RoPE table
 // (ctx * hs floats) in place, allocates the activations, caches and state, and captures the step graphs.
 // Returns m, or null after set_error() (m is freed).
@@ -485,7 +523,7 @@ static Model *finish_load(Model *m, const std::vector<float> &rope, const char *
     if ((e = cudaMalloc(&m->x, dim * 4)) != cudaSuccess || (e = cudaMalloc(&m->xb, dim * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->qkv, (dim + 2 * kv) * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->hb, (size_t)hid * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->logits, (size_t)c.head_k * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&m->logits, (size_t)c.vocab_size * 4)) != cudaSuccess ||  // room for a full head
         (e = cudaMalloc(&m->kcache, kvbytes)) != cudaSuccess || (e = cudaMalloc(&m->vcache, kvbytes)) != cudaSuccess ||
         (e = cudaMalloc(&m->rope, rope.size() * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->xq_n, dim)) != cudaSuccess || (e = cudaMalloc(&m->xs_n, dim / 32 * 4)) != cudaSuccess ||
@@ -508,33 +546,7 @@ static Model *finish_load(Model *m, const std::vector<float> &rope, const char *
         e = cudaErrorUnknown;
         return fail("expf table");
     }
-    // capture one forward step, then the instrumented copy (events between kernels, no programmatic overlap)
-    for (int pass = 0; pass < 2; pass++) {
-        cudaGraph_t graph;
-        int count = 0;
-        const bool pdl = m->pdl;
-        if (pass == 1) {
-            m->pdl = false;
-            m->prof_ev.resize(m->kernels_per_step + 1);
-            for (auto &ev : m->prof_ev)
-                if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail("events");
-        }
-        if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
-            return fail("capture");
-        cudaError_t le = pass == 0 ? enqueue_step(*m, &count, nullptr, &m->info)
-                                   : enqueue_step(*m, &count, m->prof_ev.data(), nullptr);
-        e = cudaStreamEndCapture(m->stream, &graph);
-        m->pdl = pdl;
-        if (le != cudaSuccess) {
-            e = le;
-            return fail("kernel launch");
-        }
-        if (e != cudaSuccess) return fail("capture");
-        e = cudaGraphInstantiate(pass == 0 ? &m->graph : &m->prof_graph, graph, 0);
-        cudaGraphDestroy(graph);
-        if (e != cudaSuccess) return fail("graph");
-        if (pass == 0) m->kernels_per_step = count;
-    }
+    if ((e = capture_graphs(m)) != cudaSuccess) return fail("capture");
     return m;
 }
 
@@ -662,7 +674,9 @@ extern "C" void *mvb_qwen_load(const void *image, size_t bytes, int ctx) {
         for (auto &x : v) dst.push_back(Mat{at(x.w), at(x.s)});
     };
     conv(q, m->wq); conv(k, m->wk); conv(vv, m->wv); conv(o, m->wo); conv(g, m->w1); conv(dn, m->w2); conv(u, m->w3);
-    m->head = Mat{at(hd[0].w), at(hd[0].s)};
+    m->head = m->head_trim = Mat{at(hd[0].w), at(hd[0].s)};
+    m->ids_trim = m->head_ids;
+    m->head_rows = c.head_k;
     m->emb = Mat{at(em[0].w), at(em[0].s)};
     // RoPE table, exactly qwen.c:504-508 per position
     std::vector<float> rope((size_t)m->ctx * m->hs);
@@ -790,6 +804,7 @@ extern "C" void *mvb_runq_load(const void *image, size_t bytes, int ctx) {
     conv(q, m->wq); conv(k, m->wk); conv(vv, m->wv); conv(o, m->wo); conv(w1, m->w1); conv(w2, m->w2); conv(w3, m->w3);
     m->emb = Mat{at(em[0].q), at(em[0].s)};
     m->head = Mat{at(cls[0].q), at(cls[0].s)};
+    m->head_rows = c.vocab_size;
     // RoPE table per position, computed as runq.c:506-512 does it (float powf/cosf/sinf of the host C library);
     // pair j of a head is (2j, 2j + 1), whose head_dim is 2j
     std::vector<float> rope((size_t)m->ctx * hs);
@@ -820,9 +835,33 @@ extern "C" int mvb_qwen_config(void *model, int *out) {
     Model *m = static_cast<Model *>(model);
     if (!m || !out) return -1;
     const Config &c = m->c;
-    const int v[] = {c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab_size, c.head_k, m->ctx,
+    const int v[] = {c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab_size, m->head_rows, m->ctx,
                      m->kernels_per_step};
     memcpy(out, v, sizeof v);
+    return 0;
+}
+
+// Switches a .qwb model's head between the file's trimmed head (head_k rows, ids through head_ids; qwen.c's) and
+// the full vocabulary: Qwen2 ties the output head to the token embedding (gguf2qwb.py takes the trimmed head's
+// rows from it), so the Q8 embedding serves as a vocab_size-row head whose argmax row is the token id. Recaptures
+// the step graphs; the KV cache and state are kept. 0, or -1.
+extern "C" int mvb_qwen_full_head(void *model, int on) {
+    Model *m = static_cast<Model *>(model);
+    if (!m) return -1;
+    if (m->family == kRunq) {  // runq.c's classifier already has a row per token
+        if (on) return 0;
+        set_error("mvb_qwen_full_head: a runq model has no trimmed head");
+        return -1;
+    }
+    if (wait_stream(*m, "mvb_qwen_full_head", timeout_s())) return -1;
+    m->head = on ? m->emb : m->head_trim;
+    m->head_ids = on ? nullptr : m->ids_trim;
+    m->head_rows = on ? m->c.vocab_size : m->c.head_k;
+    const cudaError_t e = capture_graphs(m);
+    if (e != cudaSuccess) {
+        set_error("mvb_qwen_full_head: capture: %s", cudaGetErrorString(e));
+        return -1;
+    }
     return 0;
 }
 
@@ -863,7 +902,7 @@ extern "C" int mvb_qwen_forward(void *model, int token, int pos, float *logits) 
         return -1;
     }
     if (set_state(*m, token, pos, -1) || mvb_qwen_launch(m, 1)) return -1;
-    if (logits && cudaMemcpyAsync(logits, m->logits, (size_t)m->c.head_k * 4, cudaMemcpyDeviceToHost, m->stream) !=
+    if (logits && cudaMemcpyAsync(logits, m->logits, (size_t)m->head_rows * 4, cudaMemcpyDeviceToHost, m->stream) !=
                       cudaSuccess) {
         set_error("mvb_qwen_forward: logits download failed");
         return -1;
