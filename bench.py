@@ -674,7 +674,8 @@ print(",".join(map(str, ids)))
 
 def runq_mode(args):
     """Configs 1 and 2: runq.c's int8 models (stories15M / stories110M architectures, synthetic seeded weights,
-    gs 32, shared classifier) decoded on the device (mvb_runq_load + the captured step graph). One step = the rest
+    group size --gs (32, as the configs state; 64 is what tools/bin2q80.py gives stories110M), shared classifier)
+    decoded on the device (mvb_runq_load + the captured step graph). One step = the rest
     of a 256-position run after the 4-token prompt (253 greedy tokens, positions 3 .. 255).
       value        device time of K steps (rewind to position 3 + 253 graph launches), L2 warm: the model is smaller
                    than the 126 MB L2, so a token's weights mostly stay there between tokens, as in a real decode
@@ -693,10 +694,11 @@ def runq_mode(args):
     for name in names:
         cfg_name, arch = RUNQ_MODELS[name]
         cfg = getattr(qwb, cfg_name)
-        path = os.path.join(DATA, f"{name}_s3.bin")
+        gs = args.gs
+        path = os.path.join(DATA, f"{name}_g{gs}_s3.bin")
         if not os.path.exists(path):
             os.makedirs(DATA, exist_ok=True)
-            qwb.write_synthetic_runq(path + ".tmp", cfg, seed=3, gs=32)
+            qwb.write_synthetic_runq(path + ".tmp", cfg, seed=3, gs=gs)
             os.replace(path + ".tmp", path)
         prompt = [int(t) for t in np.random.default_rng(4).integers(3, cfg["vocab_size"], RUNQ_PROMPT)]
         npos = 256
@@ -763,7 +765,7 @@ def runq_mode(args):
                 "ms_per_step": round(1000.0 * t_dev / args.steps, 4),
                 "us_per_token": round(1e6 * t_dev / args.steps / gen, 2),
                 "higher_is_better": True, "dtype": "int8->int32, fp32", "data": "synthetic",
-                "config": {"workload": f"{arch} architecture via runq (synthetic seeded runq v2 Q8_0, gs 32, shared "
+                "config": {"workload": f"{arch} architecture via runq (synthetic seeded runq v2 Q8_0, gs {gs}, shared "
                                        f"classifier), 4-token prompt, {gen} greedy tokens per step", "model": cfg,
                            "l2": "warm (weights fit in the 126 MB L2); 'flushed' gives the L2-flushed figure"},
                 "flushed": {"value": round(gen / t_flush, 1), "unit": "tok/s",
@@ -786,6 +788,7 @@ def main():
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
     ap.add_argument("--model", default="", choices=["", *RUNQ_MODELS], help="runq: only this model")
     ap.add_argument("--full-head", action="store_true", help="step: the full-vocabulary head (mvb_qwen_full_head)")
+    ap.add_argument("--gs", type=int, default=32, choices=[32, 64], help="runq: group size of the checkpoint")
     ap.add_argument("--mode", default="decode",
                     choices=["decode", "sweep", "sharded", "prefill", "prompt", "step", "runq"],
                     help="decode (the benchmark line), sweep (isolated matvec shapes), sharded (row-sharded matvec), "

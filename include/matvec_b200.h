@@ -64,8 +64,8 @@ void *mvb_qwen_load_file(const char *path, int ctx);
 /* Loads a runq version 2 checkpoint (the whole file's bytes, runq.c:318-357: int8 weights with fp32 scales,
  * shared or separate classifier) to the current device, each tensor in its own aligned slot, and captures the
  * decode step with runq.c's arithmetic (its quantize, rmsnorm eps 1e-5, interleaved RoPE, no biases, greedy
- * argmax over the classifier). Needs group size 32 and head size 32, 48 or 64 (group size 64 models run through
- * fpga_matvec). ctx is clipped to the header's seq_len. Returns a decoder handle, or NULL with the reason. */
+ * argmax over the classifier). Needs group size 32 or 64 (the two runq.c's FPGA build accepts) and head size 32,
+ * 48 or 64. ctx is clipped to the header's seq_len. Returns a decoder handle, or NULL with the reason. */
 void *mvb_runq_load(const void *checkpoint, size_t bytes, int ctx);
 
 /* mvb_runq_load of the checkpoint file at `path`, mapped read-only (no host copy). */

@@ -42,20 +42,21 @@ struct State {
 
 __device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 
-// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of 32 like qwen.c:355-364 (FAM kQwen) or
-// runq.c:244-270 (kRunq) into a CTA's activation planes (matvec_kernels.cuh layout: for int4 weights even/odd
-// element planes, for int8 weights chunk planes) and the scales into xs. Eight threads share a group, four
-// consecutive elements each, so one pass of the CTA covers 32 groups. The group maximum is taken over the float
-// bits of |v| (order-free and exact; NaN counts as 0, since qwen.c's fmaxf and runq.c's `>` ignore NaN),
-// combined across the eight threads with three shuffles.
-template <int BITS, int FAM>
+// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of GS (32, or 64 for runq) like
+// qwen.c:355-364 (FAM kQwen) or runq.c:244-270 (kRunq) into a CTA's activation planes (matvec_kernels.cuh
+// layout: for int4 weights even/odd element planes, for int8 weights chunk planes) and the scales into xs.
+// GS/4 threads share a group, four consecutive elements each. The group maximum is taken over the float bits of
+// |v| (order-free and exact; NaN counts as 0, since qwen.c's fmaxf and runq.c's `>` ignore NaN), combined across
+// the group's threads with shuffles.
+template <int BITS, int FAM, int GS>
 __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs) {
-    const int ng = n / 32, l = threadIdx.x & 7;
-    for (int base = 0; base < ng; base += kThreads / 8) {  // the same trip count in every thread (shuffles)
-        const int g = base + (threadIdx.x >> 3);
+    constexpr int TPG = GS / 4;  // threads per group
+    const int ng = n / GS, l = threadIdx.x % TPG;
+    for (int base = 0; base < ng; base += kThreads / TPG) {  // the same trip count in every thread (shuffles)
+        const int g = base + threadIdx.x / TPG;
         const bool on = g < ng;
         float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (on) f = reinterpret_cast<const float4 *>(v + 32 * g)[l];
+        if (on) f = reinterpret_cast<const float4 *>(v + GS * g)[l];
         auto bits = [](float x) {
             const float a = fabsf(x);
             return a == a ? __float_as_uint(a) : 0u;
@@ -64,6 +65,7 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        if (TPG == 16) m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
         float scale;
         uint32_t q0, q1, q2, q3;
         if (FAM == kRunq) {  // runq.c: scale = wmax / 127, q = round(x / scale), no guard for a zero scale
@@ -95,27 +97,31 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
     }
 }
 
-// Quantizes v[0 .. n-1] (shared memory) per group of 32 like qwen.c:355-364 (FAM kQwen) or runq.c:244-270
+// Quantizes v[0 .. n-1] (shared memory) per group of GS like qwen.c:355-364 (FAM kQwen) or runq.c:244-270
 // (kRunq) into xq/xs (global); whole CTA.
-template <int FAM>
+template <int FAM, int GS>
 __device__ __forceinline__ void quantize_to_global(const float *v, int n, int8_t *xq, float *xs) {
-    for (int g = threadIdx.x; g < n / 32; g += blockDim.x) {
-        int8_t q[32];
-        xs[g] = quantize_group<32>(v, g, FAM, q);
-        uint32_t w[8];
+    for (int g = threadIdx.x; g < n / GS; g += blockDim.x) {
+        int8_t q[GS];
+        xs[g] = quantize_group<GS>(v, g, FAM, q);
+        uint4 *dst = reinterpret_cast<uint4 *>(xq + GS * g);
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-            w[j] = (uint32_t)(uint8_t)q[4 * j] | (uint32_t)(uint8_t)q[4 * j + 1] << 8 |
-                   (uint32_t)(uint8_t)q[4 * j + 2] << 16 | (uint32_t)(uint8_t)q[4 * j + 3] << 24;
-        uint4 *dst = reinterpret_cast<uint4 *>(xq + 32 * g);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        for (int c = 0; c < GS / 16; c++) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int e = 16 * c + 4 * j;
+                w[j] = (uint32_t)(uint8_t)q[e] | (uint32_t)(uint8_t)q[e + 1] << 8 | (uint32_t)(uint8_t)q[e + 2] << 16 |
+                       (uint32_t)(uint8_t)q[e + 3] << 24;
+            }
+            dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
     }
 }
 
 // rmsnorm (qwen.c:337-344; runq.c:394-407 is the same sequence) of xv (shared memory, n floats) with weight w,
-// then quantize into xq/xs; whole CTA. xb is n floats of shared scratch.
-template <int FAM>
+// then quantize per group of GS into xq/xs; whole CTA. xb is n floats of shared scratch.
+template <int FAM, int GS>
 __device__ __forceinline__ void rmsnorm_quantize(const float *xv, float *xb, const float *w, float eps, int n,
                                                  int8_t *xq, float *xs) {
     __shared__ float s_inv;
@@ -132,7 +138,7 @@ __device__ __forceinline__ void rmsnorm_quantize(const float *xv, float *xb, con
     const float s = s_inv;
     for (int j = threadIdx.x; j < n; j += blockDim.x) xb[j] = __fmul_rn(w[j], __fmul_rn(s, xv[j]));
     __syncthreads();
-    quantize_to_global<FAM>(xb, n, xq, xs);
+    quantize_to_global<FAM, GS>(xb, n, xq, xs);
 }
 
 // Once every CTA of the grid has called this (after its global writes), returns true in exactly one CTA: the
@@ -150,17 +156,17 @@ __device__ __forceinline__ bool last_cta(int *counter) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// embedding row of the current token (qwen.c:498-501 with fp16 scales, runq.c:490-492 with fp32 scales), exact in
-// fp32; also clears the head's argmax key.
+// embedding row of the current token (qwen.c:498-501 with fp16 scales per 32, runq.c:490-492 with fp32 scales per
+// group of gs), exact in fp32; also clears the head's argmax key.
 template <int FAM>
-__global__ void embed_kernel(const int8_t *emb_q, const void *emb_s, float *x, int dim, State *st) {
+__global__ void embed_kernel(const int8_t *emb_q, const void *emb_s, float *x, int dim, int gs, State *st) {
     allow_consumer();
     wait_for_producer();
     const int tok = __ldcg(&st->token);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i == 0) st->key = 0ull;
     if (i < dim) {
-        const size_t r = (size_t)tok * dim, g = (r + i) / 32;
+        const size_t r = (size_t)tok * dim, g = (r + i) / gs;
         const float s = FAM == kRunq ? static_cast<const float *>(emb_s)[g]
                                      : scale_from_f16(static_cast<const uint16_t *>(emb_s)[g]);
         x[i] = __fmul_rn(__int2float_rn(emb_q[r + i]), s);
@@ -212,13 +218,20 @@ struct DecodeParams {
     int cap;
 };
 
-template <int BITS, int FAM, int EPI, int PRO, int TAIL, int UPT>
+// Activation planes of a decode matvec CTA: even/odd element planes for int4 weights, one plane per 16-byte chunk
+// of a group for int8 weights (n bytes either way).
+template <int BITS, int GS>
+__host__ __device__ constexpr int activation_planes() { return BITS == 4 ? 2 : GS / 16; }
+
+template <int BITS, int FAM, int GS, int EPI, int PRO, int TAIL, int UPT>
 __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodeParams p) {
     static_assert(FAM == kQwen || BITS == 8, "runq weights are int8");
-    constexpr int GB = BITS == 4 ? 16 : 32;
+    static_assert(GS == 32 || (GS == 64 && BITS == 8), "groups of 32, or 64 for int8 weights");
+    constexpr int GB = GS * BITS / 8;  // weight bytes per group
     constexpr int WC = GB / 16;
+    constexpr int XP = activation_planes<BITS, GS>();
     extern __shared__ __align__(16) uint8_t smem[];
-    const int n = p.n, ng = n / 32, tid = threadIdx.x;
+    const int n = p.n, ng = n / GS, tid = threadIdx.x;
     const int row0 = blockIdx.x * p.rt;
     const int rows = min(p.rt, p.d - row0);
     const int vrows = EPI == kEpiSwiGLU ? 2 * rows : rows;
@@ -269,14 +282,14 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     // 2. this kernel's int8 input in shared-memory planes: from the previous kernel's int8 output, or quantized
     //    (after an rmsnorm) from its fp32 output by this CTA
     uint4 *xplane = reinterpret_cast<uint4 *>(smem);
-    float *xs_s = reinterpret_cast<float *>(xplane + 2 * ng);
+    float *xs_s = reinterpret_cast<float *>(xplane + XP * ng);
     int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
     float *prod = reinterpret_cast<float *>(xsum_s + ng);
     const int ps = prod_stride(ng);
     if (PRO == kProQuantized) {
         for (int c = tid; c < n / 16; c += kThreads) {
             const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p.xq) + c);
-            const int g = c >> 1, k = c & 1;
+            const int g = c / (GS / 16), k = c % (GS / 16);
             if (BITS == 4) {
                 uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
                 uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
@@ -295,7 +308,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         // pointer that went through an integer cast would be generic, and the in-order sum would run at the
         // generic load's latency)
         const size_t stage =
-            (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
+            (size_t)XP * ng * 16 + (size_t)ng * 8 + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
         float *xv = reinterpret_cast<float *>(smem + ((stage + 15) & ~(size_t)15));
         for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
         __syncthreads();
@@ -321,7 +334,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             __syncthreads();
             qsrc = xn;
         }
-        quantize_to_planes<BITS, FAM>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
+        quantize_to_planes<BITS, FAM, GS>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
     }
     __syncthreads();
     if (BITS == 4) {
@@ -361,7 +374,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                 acc -= 8 * xsum_s[g];
             } else {
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < WC; c++) {
                     const uint4 a = xplane[c * ng + g];
                     acc = __dp4a((int)wv[k][c].x, (int)a.x, acc);
                     acc = __dp4a((int)wv[k][c].y, (int)a.y, acc);
@@ -420,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     float *sm = reinterpret_cast<float *>(smem);
     if (TAIL == kTailNormQuant) {
         for (int j = tid; j < p.d / 4; j += kThreads) reinterpret_cast<float4 *>(sm)[j] = ld_cg4(p.out + 4 * j);
-        rmsnorm_quantize<FAM>(sm, sm + p.d, p.tail_norm, p.eps, p.d, p.tail_xq, p.tail_xs);
+        rmsnorm_quantize<FAM, GS>(sm, sm + p.d, p.tail_norm, p.eps, p.d, p.tail_xq, p.tail_xs);
     } else if (TAIL == kTailNextToken && tid == 0) {
         State *st = p.st;
         const int pos = st->pos;
@@ -443,12 +456,12 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     }
 }
 
-// Dynamic shared memory of decode_matvec_kernel: the product stage (plus x and the normalized x for an rmsnorm
-// prologue), or the tail's staging if larger.
-inline size_t decode_smem_bytes(int n, int rt, int epi, int pro, int tail, int d) {
-    const int ng = n / 32;
+// Dynamic shared memory of decode_matvec_kernel for groups of gs: the product stage (plus x and the normalized x
+// for an rmsnorm prologue), or the tail's staging if larger. The activation planes take n bytes for every format.
+inline size_t decode_smem_bytes(int n, int gs, int rt, int epi, int pro, int tail, int d) {
+    const int ng = n / gs;
     const int vmax = epi == kEpiSwiGLU ? 2 * rt : rt;
-    size_t b = (size_t)2 * ng * 16 + (size_t)ng * 8 + (size_t)vmax * prod_stride(ng) * 4;
+    size_t b = (size_t)n + (size_t)ng * 8 + (size_t)vmax * prod_stride(ng) * 4;
     if (pro != kProQuantized) b = ((b + 15) & ~(size_t)15) + (size_t)(pro == kProNorm ? 2 : 1) * n * 4;
     size_t t = tail == kTailNormQuant ? (size_t)2 * d * 4 : 0;
     return b > t ? b : t;

@@ -178,19 +178,19 @@ static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
-// Rows per tile for a decode matvec: `target`, or fewer so that the tile's groups fit UPT per thread.
-static int decode_rt(int target, int n, int upt, bool pair) {
-    const int per_row = (n / 32) * (pair ? 2 : 1);
+// Rows per tile for a decode matvec: `target`, or fewer so that the tile's groups (of gs) fit UPT per thread.
+static int decode_rt(int target, int n, int gs, int upt, bool pair) {
+    const int per_row = (n / gs) * (pair ? 2 : 1);
     const int lim = kThreads * upt / per_row;
     return target < lim ? target : lim;
 }
 
-template <int BITS, int FAM, int EPI, int PRO, int TAIL, int UPT>
+template <int BITS, int FAM, int GS, int EPI, int PRO, int TAIL, int UPT>
 static cudaError_t launch_decode(Model &m, DecodeParams p, int *count) {
-    const size_t smem = decode_smem_bytes(p.n, p.rt, EPI, PRO, TAIL, p.d);
+    const size_t smem = decode_smem_bytes(p.n, GS, p.rt, EPI, PRO, TAIL, p.d);
     p.counter = m.counters + *count;
     (*count)++;
-    return launch(decode_matvec_kernel<BITS, FAM, EPI, PRO, TAIL, UPT>, dim3((p.d + p.rt - 1) / p.rt),
+    return launch(decode_matvec_kernel<BITS, FAM, GS, EPI, PRO, TAIL, UPT>, dim3((p.d + p.rt - 1) / p.rt),
                   dim3(kThreads), smem, m.stream, m.pdl, p);
 }
 
@@ -226,11 +226,14 @@ static cudaError_t launch_attention(Model &m, const AttnParams &a) {
 // kernel k and ev[count] after the last one; `info` receives each kernel's kind and layer; with `trace`, the
 // residual stream x is copied out after the embedding (slot 0) and after each layer's attention (2l + 1) and FFN
 // (2l + 2). The kernel sequence is the same for both families (qwen.c:490-573, runq.c:477-614); they differ in
-// the weight format (Q4 + fp16 scales vs Q8 + fp32 scales), the quantization rule, RoPE, biases and the head.
-template <int FAM>
+// the weight format (Q4 + fp16 scales vs Q8 + fp32 scales), the group size (32; runq also 64), the quantization
+// rule, RoPE, biases and the head.
+template <int FAM, int GS>
 static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, std::vector<Model::Info> *info,
                                        float *trace) {
     constexpr int BITS = FAM == kQwen ? 4 : 8;  // layer matrices
+    // groups per thread: a group of 64 carries twice the bytes of a group of 32, so half as many fit the registers
+    constexpr int U1 = 1, U4 = GS == 64 ? 2 : 4, U5 = GS == 64 ? 3 : 5;
     const Config &c = m.c;
     cudaError_t e;
     *count = 0;
@@ -247,7 +250,7 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
     const int dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, L = c.n_layers;
     if ((e = mark("embed", -1)) != cudaSuccess) return e;
     e = launch(embed_kernel<FAM>, dim3((dim + kThreads - 1) / kThreads), dim3(kThreads), 0, m.stream, m.pdl,
-               (const int8_t *)m.emb.w, m.emb.s, m.x, dim, m.st);
+               (const int8_t *)m.emb.w, m.emb.s, m.x, dim, GS, m.st);
     (*count)++;
     if (e != cudaSuccess || (e = snap(0)) != cudaSuccess) return e;
     for (int l = 0; l < L; l++) {
@@ -256,10 +259,10 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
         p.w[0] = m.wq[l].w; p.ws[0] = m.wq[l].s; p.rows[0] = dim;
         p.w[1] = m.wk[l].w; p.ws[1] = m.wk[l].s; p.rows[1] = kv;
         p.w[2] = m.wv[l].w; p.ws[2] = m.wv[l].s; p.rows[2] = kv;
-        p.n = dim; p.d = dim + 2 * kv; p.rt = decode_rt(8, dim, 1, false);
+        p.n = dim; p.d = dim + 2 * kv; p.rt = decode_rt(8, dim, GS, U1, false);
         p.src = m.x; p.norm_w = m.attn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.qkv; p.st = m.st;
         if ((e = mark("qkv", l)) != cudaSuccess ||
-            (e = launch_decode<BITS, FAM, kEpiStore, kProNorm, kTailNone, 1>(m, p, count)) != cudaSuccess)
+            (e = launch_decode<BITS, FAM, GS, kEpiStore, kProNorm, kTailNone, U1>(m, p, count)) != cudaSuccess)
             return e;
         // attention
         AttnParams a = {};
@@ -276,41 +279,41 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
         // o: quantize the attention output in every CTA, x += wo * it
         p = DecodeParams{};
         p.w[0] = m.wo[l].w; p.ws[0] = m.wo[l].s; p.rows[0] = dim;
-        p.n = dim; p.d = dim; p.rt = decode_rt(8, dim, 1, false);
+        p.n = dim; p.d = dim; p.rt = decode_rt(8, dim, GS, U1, false);
         p.src = m.xb; p.out = m.x; p.st = m.st;
         if ((e = mark("o_proj", l)) != cudaSuccess ||
-            (e = launch_decode<BITS, FAM, kEpiResidual, kProQuant, kTailNone, 1>(m, p, count)) != cudaSuccess ||
+            (e = launch_decode<BITS, FAM, GS, kEpiResidual, kProQuant, kTailNone, U1>(m, p, count)) != cudaSuccess ||
             (e = snap(2 * l + 1)) != cudaSuccess)
             return e;
         // gate/up: rmsnorm + quantize of x in every CTA, paired rows, SwiGLU -> hb
         p = DecodeParams{};
         p.w[0] = m.w1[l].w; p.ws[0] = m.w1[l].s; p.rows[0] = hid;
         p.w[1] = m.w3[l].w; p.ws[1] = m.w3[l].s; p.rows[1] = hid;
-        p.n = dim; p.d = hid; p.rt = decode_rt(16, dim, 4, true);
+        p.n = dim; p.d = hid; p.rt = decode_rt(16, dim, GS, U4, true);
         p.src = m.x; p.norm_w = m.ffn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.hb; p.st = m.st;
         p.et = m.et;
         if ((e = mark("gate_up", l)) != cudaSuccess ||
-            (e = launch_decode<BITS, FAM, kEpiSwiGLU, kProNorm, kTailNone, 4>(m, p, count)) != cudaSuccess)
+            (e = launch_decode<BITS, FAM, GS, kEpiSwiGLU, kProNorm, kTailNone, U4>(m, p, count)) != cudaSuccess)
             return e;
         // down: quantize hb in every CTA, x += w2 * it; after the last layer, the last CTA normalizes x for the head
         p = DecodeParams{};
         p.w[0] = m.w2[l].w; p.ws[0] = m.w2[l].s; p.rows[0] = dim;
-        p.n = hid; p.d = dim; p.rt = decode_rt(8, hid, 5, false);
+        p.n = hid; p.d = dim; p.rt = decode_rt(8, hid, GS, U5, false);
         p.src = m.hb; p.out = m.x; p.st = m.st;
         p.tail_norm = m.out_norm; p.eps = c.rms_eps; p.tail_xq = m.xq_n; p.tail_xs = m.xs_n;
         if ((e = mark("down", l)) != cudaSuccess) return e;
-        e = l + 1 < L ? launch_decode<BITS, FAM, kEpiResidual, kProQuant, kTailNone, 5>(m, p, count)
-                      : launch_decode<BITS, FAM, kEpiResidual, kProQuant, kTailNormQuant, 5>(m, p, count);
+        e = l + 1 < L ? launch_decode<BITS, FAM, GS, kEpiResidual, kProQuant, kTailNone, U5>(m, p, count)
+                      : launch_decode<BITS, FAM, GS, kEpiResidual, kProQuant, kTailNormQuant, U5>(m, p, count);
         if (e != cudaSuccess || (e = snap(2 * l + 2)) != cudaSuccess) return e;
     }
     // head (qwen.c's trimmed Q8 head, or runq.c's classifier): logits + argmax; the last CTA picks the next token
     DecodeParams p = {};
     p.w[0] = m.head.w; p.ws[0] = m.head.s; p.rows[0] = m.head_rows;
-    p.n = dim; p.d = m.head_rows; p.rt = decode_rt(32, dim, 4, false);
+    p.n = dim; p.d = m.head_rows; p.rt = decode_rt(32, dim, GS, U4, false);
     p.xq = m.xq_n; p.xs = m.xs_n; p.out = m.logits; p.st = m.st;
     p.prompt = m.prompt; p.head_ids = m.head_ids; p.ids = m.ids; p.cap = m.ctx;
     if ((e = mark("head", -1)) != cudaSuccess ||
-        (e = launch_decode<8, FAM, kEpiHead, kProQuantized, kTailNextToken, 4>(m, p, count)) != cudaSuccess)
+        (e = launch_decode<8, FAM, GS, kEpiHead, kProQuantized, kTailNextToken, U4>(m, p, count)) != cudaSuccess)
         return e;
     if (ev) e = cudaEventRecordWithFlags(ev[*count], m.stream, cudaEventRecordExternal);
     return e;
@@ -318,20 +321,21 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
 
 static cudaError_t enqueue_step(Model &m, int *count, cudaEvent_t *ev = nullptr,
                                 std::vector<Model::Info> *info = nullptr, float *trace = nullptr) {
-    return m.family == kRunq ? enqueue_step_family<kRunq>(m, count, ev, info, trace)
-                             : enqueue_step_family<kQwen>(m, count, ev, info, trace);
+    if (m.family == kQwen) return enqueue_step_family<kQwen, 32>(m, count, ev, info, trace);
+    return m.c.group_size == 64 ? enqueue_step_family<kRunq, 64>(m, count, ev, info, trace)
+                                : enqueue_step_family<kRunq, 32>(m, count, ev, info, trace);
 }
 
 // Algorithmic bytes of kernel k of the step at position `pos`: every byte the kernel must move at least once
 // (weights and scales, activations in and out, norm weights, KV-cache rows read and written).
 static double kernel_bytes(const Model &m, int k, int pos) {
     const Config &c = m.c;
-    const double dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, ng = dim / 32;
+    const double gs = c.group_size, dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, ng = dim / gs;
     const char *kind = m.info[k].kind;
     const bool runq = m.family == kRunq;
     const double sb = runq ? 4 : 2;  // bytes per weight scale
     // one layer matrix: Q4 + fp16 scales (qwen.c) or Q8 + fp32 scales (runq.c)
-    auto mat = [&](double d, double n) { return d * n * (runq ? 1.0 : 0.5) + d * (n / 32) * sb; };
+    auto mat = [&](double d, double n) { return d * n * (runq ? 1.0 : 0.5) + d * (n / gs) * sb; };
     if (!strcmp(kind, "embed")) return dim + ng * sb + dim * 4;
     // matvecs: weights + scales, int8 input + scales, outputs (read + write for residual updates); tails: the
     // vector they normalize or quantize, the norm weight, the int8 output
@@ -732,14 +736,14 @@ extern "C" void *mvb_runq_load(const void *image, size_t bytes, int ctx) {
     c.rope_theta = 10000.0f;  // runq.c:508
     c.rms_eps = 1e-5f;        // runq.c:401
     const int hs = c.n_heads > 0 ? c.dim / c.n_heads : 0;
-    // runq.c accepts group size 32 or 64 (runq.c:335-337); this decode is built for 32 (64 runs through
-    // fpga_matvec); head sizes 32, 48 (stories15M) and 64 (stories110M)
-    if (gs != 32 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.dim % c.n_heads || c.n_heads % c.n_kv_heads ||
-        (hs != 32 && hs != 48 && hs != 64) || c.dim % 32 || c.hidden_dim % 32 || c.dim > kMaxDim ||
-        c.hidden_dim > kMaxN || c.vocab_size <= 0 || c.n_layers <= 0 || c.max_seq_len <= 0) {
+    // runq.c's FPGA build accepts group size 32 or 64 (runq.c:335-337; tools/bin2q80.py picks 64 when dim allows,
+    // else 32); head sizes 32, 48 (stories15M) and 64 (stories110M)
+    if ((gs != 32 && gs != 64) || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.dim % c.n_heads ||
+        c.n_heads % c.n_kv_heads || (hs != 32 && hs != 48 && hs != 64) || c.dim % gs || c.hidden_dim % gs ||
+        c.dim > kMaxDim || c.hidden_dim > kMaxN || c.vocab_size <= 0 || c.n_layers <= 0 || c.max_seq_len <= 0) {
         set_error("mvb_runq_load: unsupported config (group %d, dim %d, hidden %d, heads %d/%d; this decode needs "
-                  "group size 32, head size 32, 48 or 64, dim <= %d, hidden <= %d)", gs, c.dim, c.hidden_dim,
-                  c.n_heads, c.n_kv_heads, kMaxDim, kMaxN);
+                  "group size 32 or 64 dividing dim and hidden, head size 32, 48 or 64, dim <= %d, hidden <= %d)",
+                  gs, c.dim, c.hidden_dim, c.n_heads, c.n_kv_heads, kMaxDim, kMaxN);
         delete m;
         return nullptr;
     }
@@ -768,7 +772,7 @@ extern "C" void *mvb_runq_load(const void *image, size_t bytes, int ctx) {
         std::vector<MatPiece> v(count);
         for (auto &x : v) {
             x.q = piece(d * n);
-            x.s = piece(d * n / 32 * 4);
+            x.s = piece(d * n / gs * 4);
         }
         return v;
     };

@@ -69,20 +69,22 @@ def test_runq_tiny_vs_golden(tmp_path):
         dec.close()
 
 
-@pytest.mark.parametrize("cfg_name, npos, nlog", [("STORIES15M", 256, 256), ("STORIES110M", 300, 300)])
-def test_runq_stories_vs_reference(tmp_path, cfg_name, npos, nlog):
-    """Configs 1 and 2 (stories15M / stories110M architectures, gs 32, shared classifier, 4 seeded prompt ids):
-    the logits of every position bit for bit (past 256 positions the attention stages its cached values in a
-    second chunk), then the greedy ids of the whole run."""
+@pytest.mark.parametrize("cfg_name, gs, npos", [("STORIES15M", 32, 256), ("STORIES110M", 32, 300),
+                                                ("STORIES110M", 64, 160)])
+def test_runq_stories_vs_reference(tmp_path, cfg_name, gs, npos):
+    """Configs 1 and 2 (stories15M / stories110M architectures, shared classifier, 4 seeded prompt ids) at group
+    size 32, and stories110M at the group size the reference's own converter gives it (tools/bin2q80.py:44-46
+    takes 64 when it divides dim): the logits of every position bit for bit (past 256 positions the attention
+    stages its cached values in a second chunk), then the greedy ids of the whole run."""
     mvb = load_pkg()
     cfg = getattr(mvb.qwb, cfg_name)
-    path = str(tmp_path / f"{cfg_name}.bin")
-    mvb.qwb.write_synthetic_runq(path, cfg, seed=3, gs=32)
+    path = str(tmp_path / f"{cfg_name}_g{gs}.bin")
+    mvb.qwb.write_synthetic_runq(path, cfg, seed=3, gs=gs)
     prompt = [int(t) for t in np.random.default_rng(4).integers(3, cfg["vocab_size"], 4)]
     ref_ids, ref_logits = ref_greedy(path, prompt, npos, tmp_path)
     dec = mvb.RunqDecoder(path, ctx=cfg["seq_len"])
     try:
-        assert_bits(device_logits(dec, prompt, ref_ids, nlog), ref_logits[:nlog])
+        assert_bits(device_logits(dec, prompt, ref_ids, npos), ref_logits)
         got = dec.generate(prompt, npos - len(prompt) + 1)
         stop = ref_ids.index(1) if 1 in ref_ids else len(ref_ids)
         assert got.tolist() == ref_ids[:stop]
@@ -90,13 +92,14 @@ def test_runq_stories_vs_reference(tmp_path, cfg_name, npos, nlog):
         dec.close()
 
 
-def test_runq_grouped_query_and_separate_classifier(tmp_path):
+@pytest.mark.parametrize("gs", [32, 64])
+def test_runq_grouped_query_and_separate_classifier(tmp_path, gs):
     """Fewer kv heads than query heads (kv_mul 2, runq.c:483-484), head size 48, and a classifier stored apart from
-    the embedding (shared_classifier 0, runq.c:315)."""
+    the embedding (shared_classifier 0, runq.c:315), at both group sizes."""
     mvb = load_pkg()
     cfg = dict(dim=192, hidden_dim=512, n_layers=3, n_heads=4, n_kv_heads=2, vocab_size=1000, seq_len=128)
     path = str(tmp_path / "gqa.bin")
-    mvb.qwb.write_synthetic_runq(path, cfg, seed=8, gs=32, shared=False)
+    mvb.qwb.write_synthetic_runq(path, cfg, seed=8, gs=gs, shared=False)
     prompt = [5, 77, 901, 12, 400]
     ref_ids, ref_logits = ref_greedy(path, prompt, 40, tmp_path)
     dec = mvb.RunqDecoder(path, ctx=128)
@@ -135,10 +138,10 @@ def test_runq_load_rejections(tmp_path):
         mvb.RunqDecoder(b"XXXX" + data[4:], ctx=32)
     with pytest.raises(mvb.MatvecError, match="not a runq version 2"):
         mvb.RunqDecoder(data[:100], ctx=32)
-    g64 = str(tmp_path / "g64.bin")
-    mvb.qwb.write_synthetic_runq(g64, mvb.qwb.RUNQ_TINY, seed=1, gs=64)
-    with pytest.raises(mvb.MatvecError, match="group size 32"):
-        mvb.RunqDecoder(g64, ctx=32)
+    g16 = str(tmp_path / "g16.bin")
+    mvb.qwb.write_synthetic_runq(g16, mvb.qwb.RUNQ_TINY, seed=1, gs=16)  # runq.c's FPGA build refuses it too
+    with pytest.raises(mvb.MatvecError, match="group size 32 or 64"):
+        mvb.RunqDecoder(g16, ctx=32)
     with pytest.raises(mvb.MatvecError, match="cannot map"):
         mvb.RunqDecoder(str(tmp_path / "missing.bin"), ctx=32)
     # a .qwb is not a runq checkpoint, and the other way round
