@@ -97,6 +97,68 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
     }
 }
 
+// Quantizes a long v[0 .. n-1] (more groups of 32 than one pass of quantize_to_planes covers) into the same
+// planes: four threads per group, eight consecutive elements each, and two groups per thread at a time, so the
+// 152 groups of a 4,864-wide input take two passes instead of five. Same arithmetic as quantize_to_planes.
+template <int BITS, int FAM>
+__device__ __forceinline__ void quantize_to_planes_wide(const float *v, int n, uint8_t *planes, float *xs) {
+    constexpr int kPass = kThreads / 4;  // groups per pass and per slot
+    const int ng = n / 32, l = threadIdx.x & 3;
+    for (int base = 0; base < ng; base += 2 * kPass) {  // the same trip count in every thread (shuffles)
+        float4 f[2][2];
+        unsigned m[2];
+        int g[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            g[h] = base + h * kPass + (threadIdx.x >> 2);
+            const bool on = g[h] < ng;
+            const float4 *src = reinterpret_cast<const float4 *>(v + 32 * g[h] + 8 * l);
+            f[h][0] = on ? src[0] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            f[h][1] = on ? src[1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            auto bits = [](float x) {
+                const float a = fabsf(x);
+                return a == a ? __float_as_uint(a) : 0u;
+            };
+            m[h] = max(max(max(bits(f[h][0].x), bits(f[h][0].y)), max(bits(f[h][0].z), bits(f[h][0].w))),
+                       max(max(bits(f[h][1].x), bits(f[h][1].y)), max(bits(f[h][1].z), bits(f[h][1].w))));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            m[h] = max(m[h], __shfl_xor_sync(0xffffffffu, m[h], 1));
+            m[h] = max(m[h], __shfl_xor_sync(0xffffffffu, m[h], 2));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            if (g[h] >= ng) continue;
+            const float e[8] = {f[h][0].x, f[h][0].y, f[h][0].z, f[h][0].w, f[h][1].x, f[h][1].y, f[h][1].z,
+                                f[h][1].w};
+            uint32_t q[8];
+            float scale;
+            if (FAM == kRunq) {  // runq.c: scale = wmax / 127, q = round(x / scale), no guard for a zero scale
+                scale = __fdiv_rn(__uint_as_float(m[h]), 127.0f);
+#pragma unroll
+                for (int i = 0; i < 8; i++) q[i] = (uint8_t)to_int8_x86(roundf(__fdiv_rn(e[i], scale)));
+            } else {
+                scale = __fmul_rn(__uint_as_float(m[h]), 1.0f / 127.0f);
+                const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, same value
+#pragma unroll
+                for (int i = 0; i < 8; i++) q[i] = (uint8_t)to_int8_x86(roundf(__fmul_rn(e[i], inv)));
+            }
+            if (BITS == 4) {
+                // elements 8l + 2i are even-plane bytes 4l + i; elements 8l + 2i + 1 odd-plane bytes 4l + i
+                *reinterpret_cast<uint32_t *>(planes + g[h] * 16 + 4 * l) = q[0] | q[2] << 8 | q[4] << 16 | q[6] << 24;
+                *reinterpret_cast<uint32_t *>(planes + (ng + g[h]) * 16 + 4 * l) =
+                    q[1] | q[3] << 8 | q[5] << 16 | q[7] << 24;
+            } else {
+                // elements 8l .. 8l+7 are bytes 8(l & 1) .. of chunk l >> 1
+                *reinterpret_cast<uint2 *>(planes + ((l >> 1) * ng + g[h]) * 16 + 8 * (l & 1)) =
+                    make_uint2(q[0] | q[1] << 8 | q[2] << 16 | q[3] << 24, q[4] | q[5] << 8 | q[6] << 16 | q[7] << 24);
+            }
+            if (l == 0) xs[g[h]] = scale;
+        }
+    }
+}
+
 // Quantizes v[0 .. n-1] (shared memory) per group of GS like qwen.c:355-364 (FAM kQwen) or runq.c:244-270
 // (kRunq) into xq/xs (global); whole CTA.
 template <int FAM, int GS>
@@ -334,7 +396,10 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             __syncthreads();
             qsrc = xn;
         }
-        quantize_to_planes<BITS, FAM, GS>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
+        if (GS == 32 && ng > kThreads / 8)
+            quantize_to_planes_wide<BITS, FAM>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
+        else
+            quantize_to_planes<BITS, FAM, GS>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
     }
     __syncthreads();
     if (BITS == 4) {
