@@ -299,14 +299,21 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     const int vrows = EPI == kEpiSwiGLU ? 2 * rows : rows;
     const int units = vrows * ng;
 
-    // 1. this tile's weights and scales into registers: they do not depend on any earlier kernel
+    // 1. this tile's weights and scales into registers: they do not depend on any earlier kernel. Each unit's
+    //    group and product slot are found here too, so that the product loop after the wait does no division.
+    const int ps = prod_stride(ng);
     uint4 wv[UPT][WC];
     uint32_t hs[UPT];  // the scale's bits: fp16 (kQwen) or fp32 (kRunq), converted where it is used
+    int ug[UPT], uslot[UPT];  // group of the unit, and its product's index vr * ps + g
 #pragma unroll
     for (int k = 0; k < UPT; k++) {
         const int u = tid + k * kThreads;
+        ug[k] = 0;
+        uslot[k] = 0;
         if (u < units) {
             const int vr = u / ng, g = u - vr * ng;
+            ug[k] = g;
+            uslot[k] = vr * ps + g;
             int m, r;
             if (EPI == kEpiSwiGLU) {
                 m = vr < rows ? 0 : 1;
@@ -347,7 +354,6 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     float *xs_s = reinterpret_cast<float *>(xplane + XP * ng);
     int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
     float *prod = reinterpret_cast<float *>(xsum_s + ng);
-    const int ps = prod_stride(ng);
     if (PRO == kProQuantized) {
         for (int c = tid; c < n / 16; c += kThreads) {
             const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p.xq) + c);
@@ -421,9 +427,8 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     // 3. group products (matvec_kernel's arithmetic)
 #pragma unroll
     for (int k = 0; k < UPT; k++) {
-        const int u = tid + k * kThreads;
-        if (u < units) {
-            const int vr = u / ng, g = u - vr * ng;
+        if (tid + k * kThreads < units) {
+            const int g = ug[k];
             int acc = 0;
             if (BITS == 4) {
                 const uint4 e = xplane[g], o = xplane[ng + g];
@@ -448,7 +453,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                 }
             }
             const float wscale = FAM == kRunq ? __uint_as_float(hs[k]) : scale_from_f16(hs[k]);
-            prod[vr * ps + g] = __fmul_rn(__fmul_rn(__int2float_rn(acc), wscale), xs_s[g]);
+            prod[uslot[k]] = __fmul_rn(__fmul_rn(__int2float_rn(acc), wscale), xs_s[g]);
         }
     }
     __syncthreads();
