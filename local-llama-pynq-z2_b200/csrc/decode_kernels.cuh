@@ -706,7 +706,10 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
     __syncthreads();
     const float sum = s_sum;
     for (int t = tid; t <= pos; t += kThreads) att[t] = __fdiv_rn(att[t], sum);
-    allow_consumer();  // the next kernel may launch (see decode_matvec_kernel)
+    // The next kernel may launch: here for runq models; for Qwen after the weighted values below, whose serial
+    // chains the next kernel's early-resident CTAs slow down (measured: Qwen step 0.620 -> 0.607 ms when released
+    // after them; stories15M 0.115 -> 0.116 ms, so it keeps the earlier release).
+    if (FAM == kRunq) allow_consumer();
     // weighted values, in order of position, from the staged chunks
     float acc = 0.0f;
     for (int c = 0; c < nchunks; c++) {
@@ -723,6 +726,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         }
         __syncthreads();
     }
+    if (FAM == kQwen) allow_consumer();
     if (tid < HS) {
         acc = __fadd_rn(acc, __fmul_rn(att[pos], vc[tid]));
         p.xb[h * HS + tid] = acc;
