@@ -83,26 +83,40 @@ __device__ __forceinline__ float ld_f32(const void *p) {
 __device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_consumer() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Shared-memory loads by shared-window address. Volatile, so that they stay after the barriers that publish
+// the data (the compiler sees no memory access in an asm statement).
+__device__ __forceinline__ float4 lds4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float lds(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
 // ((0 + a0) + a1) + ... + a_{n-1} in order, one thread, from shared memory (a 16-byte aligned). The adds form
 // one dependent chain; the values are read in blocks of 8 two blocks ahead, which keeps the chain at the latency
 // of one fp32 add per element (measured on B200 with a runtime n: 4.2 cycles per add, against 6.1 for the plain
-// loop and 7.9 for the same loop unrolled by 8).
+// loop and 7.9 for the same loop unrolled by 8). The loads are explicit shared-memory loads, whatever address
+// space the compiler inferred for `a` where the function is inlined.
 __device__ __forceinline__ float chain_sum(const float *a, int n) {
     float s = 0.0f;
     int j = 0;
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(a);
     const int n8 = n & ~7;
     if (n8 >= 16) {
-        const float4 *a4 = reinterpret_cast<const float4 *>(a);
-        float4 b0 = a4[0], b1 = a4[1], c0 = a4[2], c1 = a4[3];
+        float4 b0 = lds4(base), b1 = lds4(base + 16), c0 = lds4(base + 32), c1 = lds4(base + 48);
         for (; j < n8; j += 8) {
             const int jn = j + 16 < n8 ? j + 16 : j;  // stays inside [0, n8)
-            const float4 d0 = a4[jn / 4], d1 = a4[jn / 4 + 1];
+            const float4 d0 = lds4(base + 4 * jn), d1 = lds4(base + 4 * jn + 16);
             s = __fadd_rn(s, b0.x); s = __fadd_rn(s, b0.y); s = __fadd_rn(s, b0.z); s = __fadd_rn(s, b0.w);
             s = __fadd_rn(s, b1.x); s = __fadd_rn(s, b1.y); s = __fadd_rn(s, b1.z); s = __fadd_rn(s, b1.w);
             b0 = c0; b1 = c1; c0 = d0; c1 = d1;
         }
     }
-    for (; j < n; j++) s = __fadd_rn(s, a[j]);
+    for (; j < n; j++) s = __fadd_rn(s, lds(base + 4 * j));
     return s;
 }
 
