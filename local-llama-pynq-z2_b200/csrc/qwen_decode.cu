@@ -22,6 +22,12 @@
 // RoPE angles from the host's double-precision pow/cos/sin exactly as qwen.c:504-508 computes them, and expf
 // (softmax, SiLU) with the host C library's exact results (expf_ref.h), so the step reproduces qwen.c's logits
 // bit for bit.
+//
+// The same runtime decodes runq.c's int8 models (mvb_runq_load): the kernel sequence is the same, with runq.c's
+// arithmetic where it differs (runq.c:477-614): int8 weights with fp32 scales in groups of 32 or 64, activation
+// quantization by division, rmsnorm eps 1e-5, interleaved RoPE from the host C library's float powf/cosf/sinf
+// (runq.c:506-521), no biases, and a classifier whose argmax row is the token (runq.c:843-854). A .qwb model can
+// also use its tied embedding as a full-vocabulary head (mvb_qwen_full_head).
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -733,10 +739,10 @@ extern "C" void *mvb_runq_load(const void *image, size_t bytes, int ctx) {
     c.dim = h[0]; c.hidden_dim = h[1]; c.n_layers = h[2]; c.n_heads = h[3]; c.n_kv_heads = h[4];
     c.vocab_size = h[5]; c.max_seq_len = h[6]; c.group_size = gs; c.emb_bits = 8;
     c.head_k = c.vocab_size;  // the classifier has a row per token
-    c.rope_theta = 10000.0f;  // runq.c:508
+    c.rope_theta = 10000.0f;  // runq.c:509
     c.rms_eps = 1e-5f;        // runq.c:401
     const int hs = c.n_heads > 0 ? c.dim / c.n_heads : 0;
-    // runq.c's FPGA build accepts group size 32 or 64 (runq.c:335-337; tools/bin2q80.py picks 64 when dim allows,
+    // runq.c's FPGA build accepts group size 32 or 64 (runq.c:339-341; tools/bin2q80.py picks 64 when dim allows,
     // else 32); head sizes 32, 48 (stories15M) and 64 (stories110M)
     if ((gs != 32 && gs != 64) || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.dim % c.n_heads ||
         c.n_heads % c.n_kv_heads || (hs != 32 && hs != 48 && hs != 64) || c.dim % gs || c.hidden_dim % gs ||
