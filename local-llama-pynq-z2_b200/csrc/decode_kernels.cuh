@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
     float *att = vc + HS;                                  // ctx scores
     float *vbuf = att + ((p.ctx + 3) & ~3);                // 2 x kVChunk x HS staged values
     __shared__ float red[kThreads / 32];
-    __shared__ float s_max, s_sum;
+    __shared__ float s_sum;
     const int h = blockIdx.x, kvh = h / p.kv_mul, half = HS / 2, tid = threadIdx.x;
     // Everything up to the wait reads only what earlier steps wrote (the position, set by the previous step's
     // head kernel; the cache rows of earlier positions) or constants (RoPE table, biases). Within one step no
@@ -664,8 +664,10 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         p.kcache[(size_t)pos * p.kv_dim + kvh * HS + tid] = kc[tid];
         p.vcache[(size_t)pos * p.kv_dim + kvh * HS + tid] = vc[tid];
     }
-    // scores: one position per thread, the head's HS products added in order
+    // scores: one position per thread, the head's HS products added in order; each thread keeps the largest of
+    // its scores for the softmax
     const float scale = __fsqrt_rn((float)HS);
+    float m = -INFINITY;
     for (int t = tid; t <= pos; t += kThreads) {
         if (t == pos) {
 #pragma unroll
@@ -683,23 +685,20 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
             score = __fadd_rn(score, __fmul_rn(q[4 * i + 2], k4[i].z));
             score = __fadd_rn(score, __fmul_rn(q[4 * i + 3], k4[i].w));
         }
-        att[t] = __fdiv_rn(score, scale);
+        const float a = __fdiv_rn(score, scale);
+        att[t] = a;
+        m = fmaxf(m, a);
     }
-    __syncthreads();
-    // softmax (qwen.c:346-352, runq.c:409-427): max, exp(x - max), in-order sum, divide
-    float m = -INFINITY;
-    for (int t = tid; t <= pos; t += kThreads) m = fmaxf(m, att[t]);
+    // softmax (qwen.c:346-352, runq.c:409-427): max (order-free: the same value as the reference's scan), exp(x -
+    // max), in-order sum, divide. Every thread combines the warps' maxima itself, and exponentiates only the
+    // scores it wrote, so one barrier serves the max.
 #pragma unroll
     for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     if ((tid & 31) == 0) red[tid >> 5] = m;
     __syncthreads();
-    if (tid == 0) {
-        float mm = red[0];
-        for (int w = 1; w < kThreads / 32; w++) mm = fmaxf(mm, red[w]);
-        s_max = mm;
-    }
-    __syncthreads();
-    const float mx = s_max;
+    float mx = red[0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; w++) mx = fmaxf(mx, red[w]);
     for (int t = tid; t <= pos; t += kThreads) att[t] = expf_ref(__fsub_rn(att[t], mx), p.et);
     __syncthreads();
     if (tid == 0) s_sum = chain_sum(att, pos + 1);
