@@ -4,10 +4,11 @@
 //      (griddepcontrol.wait), so with programmatic dependent launch these loads overlap the previous kernel;
 //   2. turns the previous kernel's fp32 output into this kernel's int8 input in every CTA at once (rmsnorm +
 //      quantize, or quantize), reading it with L2 loads;
-//   3. computes, letting the next kernel launch (griddepcontrol.launch_dependents) once its serial prologue is
-//      done. Two kernels also have a tail run by their last CTA to finish (an atomic counter that this CTA
-//      resets for the next step): the last layer's down projection normalizes x once for the 2,048-CTA head,
-//      and the head picks the next token.
+//   3. computes, letting the next kernel launch (griddepcontrol.launch_dependents) where measurement put it:
+//      for most matvecs just before the fold, for qkv at the top (its consumer, the attention, prefetches the
+//      KV cache), for the attention after its value sums (Qwen) or before them (runq). Two kernels also have a
+//      tail run by their last CTA to finish (an atomic counter that this CTA resets for the next step): the
+//      last layer's down projection normalizes x once for the head, and the head picks the next token.
 // The kernels serve two model families, chosen by the template parameter FAM:
 //   kQwen  qwen.c (qwen/qwen.c): int4/int8 weights with fp16 scales, activations quantized by the reciprocal of
 //          the scale, q/k/v biases, NeoX RoPE (pairs i, i + hs/2), a head mapped through head_ids;
@@ -280,6 +281,10 @@ struct DecodeParams {
     int cap;
 };
 
+// Bytes of a decode matvec CTA's per-group activation scales and int4 offset sums, padded to 16 so that the
+// product rows after them are 16-byte aligned.
+__host__ __device__ constexpr size_t scale_bytes(int ng) { return ((size_t)ng * 8 + 15) & ~(size_t)15; }
+
 // Activation planes of a decode matvec CTA: even/odd element planes for int4 weights, one plane per 16-byte chunk
 // of a group for int8 weights (n bytes either way).
 template <int BITS, int GS>
@@ -353,7 +358,9 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     uint4 *xplane = reinterpret_cast<uint4 *>(smem);
     float *xs_s = reinterpret_cast<float *>(xplane + XP * ng);
     int *xsum_s = reinterpret_cast<int *>(xs_s + ng);
-    float *prod = reinterpret_cast<float *>(xsum_s + ng);
+    // the products start on 16 bytes, as the fold reads them 16 bytes at a time: xs and xsum take 8 * ng bytes,
+    // padded by 8 when ng is odd
+    float *prod = reinterpret_cast<float *>(xsum_s + ng + 2 * (ng & 1));
     if (PRO == kProQuantized) {
         for (int c = tid; c < n / 16; c += kThreads) {
             const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p.xq) + c);
@@ -376,7 +383,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         // pointer that went through an integer cast would be generic, and the in-order sum would run at the
         // generic load's latency)
         const size_t stage =
-            (size_t)XP * ng * 16 + (size_t)ng * 8 + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
+            (size_t)XP * ng * 16 + scale_bytes(ng) + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
         float *xv = reinterpret_cast<float *>(smem + ((stage + 15) & ~(size_t)15));
         for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
         __syncthreads();
@@ -466,7 +473,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
 
     // 4. in-order fold of each virtual row, epilogue
     float v = 0.0f;
-    if (tid < vrows) v = chain_sum(prod + tid * ps, ng);
+    if (tid < vrows) v = chain_sum_padded(prod + tid * ps, ng);  // rows are padded to a multiple of 4
     if (EPI == kEpiStore) {
         if (tid < rows) p.out[row0 + tid] = v;
     } else if (EPI == kEpiResidual) {
@@ -531,7 +538,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
 inline size_t decode_smem_bytes(int n, int gs, int rt, int epi, int pro, int tail, int d) {
     const int ng = n / gs;
     const int vmax = epi == kEpiSwiGLU ? 2 * rt : rt;
-    size_t b = (size_t)n + (size_t)ng * 8 + (size_t)vmax * prod_stride(ng) * 4;
+    size_t b = (size_t)n + scale_bytes(ng) + (size_t)vmax * prod_stride(ng) * 4;
     if (pro != kProQuantized) b = ((b + 15) & ~(size_t)15) + (size_t)(pro == kProNorm ? 2 : 1) * n * 4;
     size_t t = tail == kTailNormQuant ? (size_t)2 * d * 4 : 0;
     return b > t ? b : t;

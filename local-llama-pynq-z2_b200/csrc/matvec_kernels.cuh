@@ -120,6 +120,43 @@ __device__ __forceinline__ float chain_sum(const float *a, int n) {
     return s;
 }
 
+// chain_sum for a row that may be read up to its next multiple of 4 floats (the product rows, whose stride has that
+// padding). The last n - n8 (< 8) values come in as up to two float4 loads issued before the blocks; their
+// addresses are clamped into the row, so every load is in range whatever n is.
+__device__ __forceinline__ float4 chain_tail_load(uint32_t base, int n8, int nt, int k) {
+    return lds4(base + 4 * (nt > 4 * k ? n8 + 4 * k : 0));
+}
+
+__device__ __forceinline__ float chain_blocks(uint32_t base, int n8, float s) {
+    if (n8 >= 16) {
+        float4 b0 = lds4(base), b1 = lds4(base + 16), c0 = lds4(base + 32), c1 = lds4(base + 48);
+        for (int j = 0; j < n8; j += 8) {
+            const int jn = j + 16 < n8 ? j + 16 : j;  // stays inside [0, n8)
+            const float4 d0 = lds4(base + 4 * jn), d1 = lds4(base + 4 * jn + 16);
+            s = __fadd_rn(s, b0.x); s = __fadd_rn(s, b0.y); s = __fadd_rn(s, b0.z); s = __fadd_rn(s, b0.w);
+            s = __fadd_rn(s, b1.x); s = __fadd_rn(s, b1.y); s = __fadd_rn(s, b1.z); s = __fadd_rn(s, b1.w);
+            b0 = c0; b1 = c1; c0 = d0; c1 = d1;
+        }
+    } else if (n8 == 8) {
+        const float4 b0 = lds4(base), b1 = lds4(base + 16);
+        s = __fadd_rn(s, b0.x); s = __fadd_rn(s, b0.y); s = __fadd_rn(s, b0.z); s = __fadd_rn(s, b0.w);
+        s = __fadd_rn(s, b1.x); s = __fadd_rn(s, b1.y); s = __fadd_rn(s, b1.z); s = __fadd_rn(s, b1.w);
+    }
+    return s;
+}
+
+__device__ __forceinline__ float chain_sum_padded(const float *a, int n) {
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(a);
+    const int n8 = n & ~7, nt = n - n8;
+    const float4 t0 = chain_tail_load(base, n8, nt, 0), t1 = chain_tail_load(base, n8, nt, 1);
+    float s = chain_blocks(base, n8, 0.0f);
+    const float tv[7] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z};
+#pragma unroll
+    for (int i = 0; i < 7; i++)
+        if (i < nt) s = __fadd_rn(s, tv[i]);
+    return s;
+}
+
 // Row stride (floats) of the product buffer for ng groups: at least ng, rows 16-byte aligned, and stride = 4 mod 32
 // words so that the 8 threads of a quarter-warp reading 16 bytes of their own rows hit distinct banks.
 __host__ __device__ constexpr int prod_stride(int ng) { return ng + ((36 - ng % 32) % 32); }
@@ -338,7 +375,7 @@ __device__ __forceinline__ void stream_tile(const MatvecParams &p, const MatvecS
     allow_consumer();
 
     // Row r's products in group order, exactly like the reference's `val += ...` loop.
-    if (tid < rows) store(row0 + tid, chain_sum(prod + tid * ps, ng));
+    if (tid < rows) store(row0 + tid, chain_sum_padded(prod + tid * ps, ng));  // rows are padded to a multiple of 4
 }
 
 // Rows [r0, r1) of CTA b of a grid over d rows: contiguous, balanced to within one row.

@@ -109,6 +109,22 @@ def test_runq_grouped_query_and_separate_classifier(tmp_path, gs):
         dec.close()
 
 
+def test_runq_odd_group_counts(tmp_path):
+    """Odd group counts per row (dim 544: 17 groups; hidden 1120: 35), whose per-CTA scale arrays need padding to
+    keep the product rows 16-byte aligned for the fold's 16-byte loads; head size 32."""
+    mvb = load_pkg()
+    cfg = dict(dim=544, hidden_dim=1120, n_layers=2, n_heads=17, n_kv_heads=17, vocab_size=700, seq_len=64)
+    path = str(tmp_path / "odd.bin")
+    mvb.qwb.write_synthetic_runq(path, cfg, seed=12, gs=32)
+    prompt = [9, 300, 41]
+    ref_ids, ref_logits = ref_greedy(path, prompt, 24, tmp_path)
+    dec = mvb.RunqDecoder(path, ctx=64)
+    try:
+        assert_bits(device_logits(dec, prompt, ref_ids, 24), ref_logits)
+    finally:
+        dec.close()
+
+
 def test_runq_bytes_and_file_loaders_agree(tmp_path):
     """mvb_runq_load (caller's bytes) and mvb_runq_load_file (mapped file) give the same model."""
     mvb = load_pkg()
