@@ -587,7 +587,21 @@ template <int HS>
 __device__ __forceinline__ float weighted_chain(float acc, const float *a, const float *vb, int nt) {
     int t = 0;
     const int n8 = nt & ~7;
-    if (n8 >= 16) {
+    // the last nt - n8 (< 8) products are formed first, off the chain (indices clamped into [0, nt))
+    float tail[7];
+#pragma unroll
+    for (int i = 0; i < 7; i++) {
+        const int j = n8 + i < nt ? n8 + i : 0;
+        tail[i] = __fmul_rn(a[j], vb[j * HS]);
+    }
+    if (n8 == 8) {
+        float p0[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) p0[i] = __fmul_rn(a[i], vb[i * HS]);
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc = __fadd_rn(acc, p0[i]);
+        t = 8;
+    } else if (n8 >= 16) {
         float p0[8], p1[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
@@ -608,7 +622,9 @@ __device__ __forceinline__ float weighted_chain(float acc, const float *a, const
             }
         }
     }
-    for (; t < nt; t++) acc = __fadd_rn(acc, __fmul_rn(a[t], vb[t * HS]));
+#pragma unroll
+    for (int i = 0; i < 7; i++)
+        if (n8 + i < nt) acc = __fadd_rn(acc, tail[i]);
     return acc;
 }
 
@@ -708,7 +724,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
     for (int w = 1; w < kThreads / 32; w++) mx = fmaxf(mx, red[w]);
     for (int t = tid; t <= pos; t += kThreads) att[t] = expf_ref(__fsub_rn(att[t], mx), p.et);
     __syncthreads();
-    if (tid == 0) s_sum = chain_sum(att, pos + 1);
+    if (tid == 0) s_sum = chain_sum_padded(att, pos + 1);  // att holds a multiple of 4 floats
     __syncthreads();
     const float sum = s_sum;
     for (int t = tid; t <= pos; t += kThreads) att[t] = __fdiv_rn(att[t], sum);
