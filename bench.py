@@ -351,11 +351,8 @@ def sweep_mode(args):
     torch.cuda.set_device(0)
     gen = torch.Generator(device="cuda").manual_seed(0)
     peak, peak_kind = peaks()
-    shapes = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 1152, 4), (896, 65536, 8),
-              (896, 151936, 8), (8192, 131072, 4)]
-    # runq's int8 weights with fp32 scales (fpga_matvec): the stories15M / stories110M shapes, group size 32
-    runq_shapes = [(288, 288), (288, 768), (768, 288), (288, 32000), (768, 768), (768, 2048), (2048, 768),
-                   (768, 32000)]
+    shapes = SWEEP_SHAPES
+    runq_shapes = SWEEP_RUNQ_SHAPES  # runq's int8 weights with fp32 scales (fpga_matvec), group size 32
     if args.only:
         shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
         runq_shapes = [sh for sh in runq_shapes if f"{sh[1]}x{sh[0]}" == args.only]
@@ -394,6 +391,80 @@ def sweep_mode(args):
         del w, sc
         torch.cuda.empty_cache()
     print(json.dumps({"mode": "sweep", "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "results": out_lines}))
+
+
+SWEEP_SHAPES = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 1152, 4), (896, 65536, 8),
+                (896, 151936, 8), (8192, 131072, 4)]  # (n columns, d rows, weight bits): fp16-scale matvecs
+SWEEP_RUNQ_SHAPES = [(288, 288), (288, 768), (768, 288), (288, 32000), (768, 768), (768, 2048), (2048, 768),
+                     (768, 32000)]  # runq's int8 weights with fp32 scales at the stories15M / stories110M shapes
+
+
+def reference_sweep(args):
+    """Config 4 on the host cores: the reference's own CPU matvec, timed per sweep shape. qwen.c's matmul_cpu
+    (qwen.c:436-456, OpenMP over rows) for the Q4/Q8 fp16-scale shapes and runq.c's matmul (runq.c:430-458) for the
+    fp32-scale shapes, both compiled unchanged into oracle/_ref/ with -O3 -fopenmp -ffp-contract=off, with every
+    host core. Weights rotate through copies that together exceed 512 MB (beyond any host's last-level cache), so
+    every call streams its matrix from DRAM, as the device sweep streams it from HBM. Each shape runs calls for
+    about a second (bounded sample) after one warm-up pass over all copies; GB/s uses the same algorithmic bytes."""
+    import ctypes as C
+    import numpy as np
+    threads = os.cpu_count()
+    os.environ["OMP_NUM_THREADS"] = str(threads)  # read by libgomp when the harness library loads below
+    libs = {name: os.path.join(ROOT, "oracle", "_ref", name) for name in ("libref_qwen.so", "libref_runq.so")}
+    if not all(os.path.exists(p) for p in libs.values()):
+        print(json.dumps({"mode": "sweep", "impl": "reference",
+                          "unavailable": "oracle/_ref was not built (the reference tree was absent at build time)"}))
+        return
+    lq, lr = C.CDLL(libs["libref_qwen.so"]), C.CDLL(libs["libref_runq.so"])
+    vp, sz = C.c_void_p, C.c_size_t
+    lq.ref_qwen_time_matmul_cpu.restype = lr.ref_runq_time_matmul_cpu.restype = C.c_double
+    lq.ref_qwen_time_matmul_cpu.argtypes = lr.ref_runq_time_matmul_cpu.argtypes = [
+        vp, vp, vp, sz, sz, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int]
+    rng = np.random.default_rng(0)
+    pool = 512 * 2**20
+    shapes = [(n, d, 8, "runq") for n, d in SWEEP_RUNQ_SHAPES] + [(n, d, b, "qwen") for n, d, b in SWEEP_SHAPES]
+    if args.only:
+        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+    wbytes_max = max(d * n * b // 8 for n, d, b, _ in shapes) if shapes else 0
+    wpool = np.frombuffer(rng.bytes(max(pool, wbytes_max)), np.uint8)  # weight bytes: uniform int4 nibbles / int8
+    # fp16 scale patterns in [1e-3, 2e-2]; fp32 scales the same range; at most 1/8 of a weight byte per weight byte
+    s16 = (rng.random(wpool.size // 8 // 2 + 1) * 0.019 + 0.001).astype(np.float16).view(np.uint16)
+    s32 = (rng.random(wpool.size // 8 // 4 + 1) * 0.019 + 0.001).astype(np.float32)
+    results = []
+    for n, d, bits, kind in shapes:
+        wbytes, ng = d * n * bits // 8, d * (n // 32)
+        copies = max(1, min(wpool.size // wbytes, 4096))
+        x = rng.standard_normal(n).astype(np.float32)
+        amax = np.abs(x.reshape(-1, 32)).max(axis=1)
+        xs = (amax / np.float32(127)).astype(np.float32)  # activations: N(0, 1) quantized per group of 32
+        xq = np.clip(np.rint(x / np.repeat(xs, 32)), -127, 127).astype(np.int8)
+        out = np.empty(d, np.float32)
+        if kind == "qwen":
+            fn, sc, scb = lq.ref_qwen_time_matmul_cpu, s16, 2
+            b = _alg_bytes(n, d, bits)
+            label = f"{d}x{n} Q{bits}"
+        else:
+            fn, sc, scb = lr.ref_runq_time_matmul_cpu, s32, 4
+            b = _alg_bytes(n, d, 8, scale_bytes=4)
+            label = f"{d}x{n} Q8 fp32-scale (runq)"
+        call = lambda reps: fn(out.ctypes.data, wpool.ctypes.data, sc.ctypes.data, wbytes, ng, copies,
+                               xq.ctypes.data, xs.ctypes.data, n, d, bits if kind == "qwen" else 32, reps)
+        t1 = call(copies) / copies  # warm-up over every copy (first touch of the pool pages)
+        reps = max(3, min(1_000_000, int(1.0 / max(t1, 1e-7))))
+        t = call(reps) / reps
+        line = {"impl": "reference", "shape": label, "us": round(t * 1e6, 3), "GBps": round(b / t / 1e9, 2),
+                "bytes": b, "copies": copies, "calls": reps}
+        results.append(line)
+        print(json.dumps(line), flush=True)
+    cpu = ""
+    try:
+        cpu = next((l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name")), "")
+    except OSError:
+        pass
+    print(json.dumps({"mode": "sweep", "impl": "reference", "cores": threads, "cpu": cpu,
+                      "sample": "the reference's matmul_cpu (qwen.c) / matmul (runq.c), -O3 -fopenmp "
+                                "-ffp-contract=off, OMP_NUM_THREADS = all host cores, about 1 s of calls per shape, "
+                                "weights rotated through >= 512 MB of copies", "results": results}))
 
 
 def prefill_mode(args):
@@ -801,6 +872,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if args.mode == "sweep":
+            if rank == 0:
+                reference_sweep(args)
+            return
         reference_arm(args, rank, world)
         return
     if args.mode == "sweep":

@@ -29,6 +29,28 @@ void ref_qwen_matmul_cpu(float *out, const uint8_t *w, const uint16_t *s, const 
     matmul_cpu(out, &m, xq, xs);
 }
 
+/* The CPU side of the isolated matvec sweep: `reps` back-to-back calls of matmul_cpu (OpenMP over rows, as qwen.c
+ * builds it), call r reading weight copy r % copies (w + c * wstride bytes, s + c * sstride scales) so that the
+ * copies can be sized past the last-level cache. Returns the wall-clock seconds of all calls. */
+double ref_qwen_time_matmul_cpu(float *out, const uint8_t *w, const uint16_t *s, size_t wstride, size_t sstride,
+                                int copies, const int8_t *xq, const float *xs, int n, int d, int bits, int reps) {
+    Matrix m;
+    memset(&m, 0, sizeof m);
+    m.n = n;
+    m.d = d;
+    m.bits = bits;
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (int r = 0; r < reps; r++) {
+        const size_t c = (size_t)(r % copies);
+        m.w = w + c * wstride;
+        m.s = s + c * sstride;
+        matmul_cpu(out, &m, xq, xs);
+    }
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
+}
+
 static Transformer model;
 static int model_open;
 

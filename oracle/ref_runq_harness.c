@@ -38,6 +38,29 @@ void ref_runq_matmul_cpu(float *out, const int8_t *wq, const float *ws, const in
     CPU_MATMUL(out, &x, &w, n, d);
 }
 
+/* The CPU side of the isolated sweep for runq's int8 / fp32-scale matvec: `reps` back-to-back calls of runq.c's
+ * CPU matmul, call r reading weight copy r % copies (wq + c * wstride values, ws + c * sstride scales). Returns
+ * the wall-clock seconds of all calls. */
+double ref_runq_time_matmul_cpu(float *out, const int8_t *wq, const float *ws, size_t wstride, size_t sstride,
+                                int copies, const int8_t *xq, const float *xs, int n, int d, int gs, int reps) {
+    QuantizedTensor x, w;
+    memset(&x, 0, sizeof x);
+    memset(&w, 0, sizeof w);
+    x.q = (int8_t *)xq;
+    x.s = (float *)xs;
+    GS = gs;
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (int r = 0; r < reps; r++) {
+        const size_t c = (size_t)(r % copies);
+        w.q = (int8_t *)wq + c * wstride;
+        w.s = (float *)ws + c * sstride;
+        CPU_MATMUL(out, &x, &w, n, d);
+    }
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
+}
+
 static Transformer model;
 static int model_open;
 

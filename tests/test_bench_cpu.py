@@ -1,0 +1,77 @@
+"""bench.py's CPU side without a GPU: the reference arm of the isolated sweep (--impl reference --mode sweep) times
+the reference's own matmul_cpu (qwen.c:436-456) and runq matmul (runq.c:430-458) through timing loops in the
+oracle harnesses. Checks that those loops compute what the plain calls compute on the last copy they read, and that
+the sweep prints well-formed lines."""
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+import oracle
+
+needs_ref = pytest.mark.skipif(not (oracle.ref_available("libref_qwen.so") and oracle.ref_available("libref_runq.so")),
+                               reason="oracle/_ref not built (the reference tree was absent at build time)")
+
+
+def _timer(lib, name):
+    fn = getattr(lib, name)
+    fn.restype = C.c_double
+    fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p,
+                   C.c_int, C.c_int, C.c_int, C.c_int]
+    return fn
+
+
+@needs_ref
+@pytest.mark.parametrize("bits", [4, 8])
+def test_qwen_timing_loop_matches_matmul_cpu(bits):
+    ref = oracle.RefQwen()
+    rng = np.random.default_rng(5)
+    n, d, copies, reps = 896, 40, 3, 5  # the last call reads copy (reps - 1) % copies = 1
+    wbytes, ng = d * n * bits // 8, d * n // 32
+    w = rng.integers(0, 256, copies * wbytes, dtype=np.uint8)
+    s = (rng.random(copies * ng) * 0.019 + 0.001).astype(np.float16).view(np.uint16)
+    xq, xs = ref.quantize(rng.standard_normal(n).astype(np.float32))
+    out = np.full(d, np.nan, np.float32)
+    t = _timer(ref.lib, "ref_qwen_time_matmul_cpu")(out.ctypes.data, w.ctypes.data, s.ctypes.data, wbytes, ng,
+                                                    copies, xq.ctypes.data, xs.ctypes.data, n, d, bits, reps)
+    assert t > 0
+    want = ref.matmul_cpu(w[wbytes:2 * wbytes], s[ng:2 * ng], xq, xs, n, d, bits)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+@needs_ref
+@pytest.mark.parametrize("gs", [32, 64])
+def test_runq_timing_loop_matches_matmul(gs):
+    ref = oracle.RefRunq()
+    rng = np.random.default_rng(6)
+    n, d, copies, reps = 768, 24, 2, 4  # the last call reads copy 1
+    ng = d * n // gs
+    wq = rng.integers(-127, 128, copies * d * n, dtype=np.int8)
+    ws = (rng.random(copies * ng) * 0.019 + 0.001).astype(np.float32)
+    xq, xs = ref.quantize(rng.standard_normal(n).astype(np.float32), gs)
+    out = np.full(d, np.nan, np.float32)
+    t = _timer(ref.lib, "ref_runq_time_matmul_cpu")(out.ctypes.data, wq.ctypes.data, ws.ctypes.data, d * n, ng,
+                                                    copies, xq.ctypes.data, xs.ctypes.data, n, d, gs, reps)
+    assert t > 0
+    want = ref.matmul_cpu(wq[d * n:], ws[ng:], xq, xs, n, d, gs)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+@needs_ref
+def test_reference_sweep_line():
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--mode", "sweep",
+                        "--only", "128x896"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(l) for l in r.stdout.strip().splitlines()]
+    summary = lines[-1]
+    assert summary["mode"] == "sweep" and summary["impl"] == "reference"
+    assert summary["cores"] == os.cpu_count()
+    (res,) = summary["results"]
+    assert res["shape"] == "128x896 Q4" and res["us"] > 0 and res["GBps"] > 0
+    assert res["bytes"] == 128 * 448 + 128 * 28 * 2 + 896 + 28 * 4 + 4 * 128
