@@ -29,7 +29,8 @@ namespace decode {
 constexpr int kQwen = kXQuantizeQwen, kRunq = kXQuantizeRunq;
 
 constexpr int kImEnd = 151645, kEndOfText = 151643;  // qwen.c:31-32
-constexpr int kMaxNormPerThread = 8;                     // rmsnorm'd vectors have at most 8 * 256 = 2048 elements
+// rmsnorm'd vectors have at most 2048 elements: two passes of quantize_to_planes (kThreads / (GS / 4) groups each)
+constexpr int kNormPasses = 2;
 
 struct State {
     int token;       // token of the current position
@@ -45,19 +46,33 @@ __device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinter
 
 // Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of GS (32, or 64 for runq) like
 // qwen.c:355-364 (FAM kQwen) or runq.c:244-270 (kRunq) into a CTA's activation planes (matvec_kernels.cuh
-// layout: for int4 weights even/odd element planes, for int8 weights chunk planes) and the scales into xs.
+// layout: for int4 weights even/odd element planes, for int8 weights chunk planes) and the scales into xs; for
+// int4 weights also each group's sum of its int8 values into xsum (the nibble offset correction of the products).
 // GS/4 threads share a group, four consecutive elements each. The group maximum is taken over the float bits of
 // |v| (order-free and exact; NaN counts as 0, since qwen.c's fmaxf and runq.c's `>` ignore NaN), combined across
 // the group's threads with shuffles.
-template <int BITS, int FAM, int GS>
-__device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs) {
+// NORM: v is an rmsnorm's input and each element is first normalized as qwen.c:343 / runq.c:406 do,
+// fl(w * fl(sc * v)), with this thread's rmsnorm weights nw0 / nw1 (the four of its elements in the first /
+// second pass, see norm_weights_for_planes) and the inverse root sc; n is then at most kNormPasses passes of groups.
+template <int BITS, int FAM, int GS, bool NORM>
+__device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs, int *xsum,
+                                                   float4 nw0, float4 nw1, float sc) {
     constexpr int TPG = GS / 4;  // threads per group
     const int ng = n / GS, l = threadIdx.x % TPG;
-    for (int base = 0; base < ng; base += kThreads / TPG) {  // the same trip count in every thread (shuffles)
+    for (int base = 0, pass = 0; base < ng; base += kThreads / TPG, pass++) {  // the same trip count in every
+                                                                               // thread (shuffles)
+        if (NORM && pass == kNormPasses) break;
         const int g = base + threadIdx.x / TPG;
         const bool on = g < ng;
         float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (on) f = reinterpret_cast<const float4 *>(v + GS * g)[l];
+        if (NORM) {
+            const float4 w = pass == 0 ? nw0 : nw1;  // a select of registers, not an indexed local array
+            f.x = __fmul_rn(w.x, __fmul_rn(sc, f.x));
+            f.y = __fmul_rn(w.y, __fmul_rn(sc, f.y));
+            f.z = __fmul_rn(w.z, __fmul_rn(sc, f.z));
+            f.w = __fmul_rn(w.w, __fmul_rn(sc, f.w));
+        }
         auto bits = [](float x) {
             const float a = fabsf(x);
             return a == a ? __float_as_uint(a) : 0u;
@@ -83,11 +98,19 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
             q2 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.z, inv)));
             q3 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.w, inv)));
         }
+        int sum = 0;
+        if (BITS == 4) {  // the group's sum of its int8 values: this thread's four, then across the group's threads
+            sum = (int)(int8_t)q0 + (int)(int8_t)q1 + (int)(int8_t)q2 + (int)(int8_t)q3;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        }
         if (on) {
             if (BITS == 4) {
                 // elements 4l, 4l+2 are even-plane bytes 2l, 2l+1; elements 4l+1, 4l+3 odd-plane bytes 2l, 2l+1
                 *reinterpret_cast<uint16_t *>(planes + g * 16 + 2 * l) = (uint16_t)(q0 | q2 << 8);
                 *reinterpret_cast<uint16_t *>(planes + (ng + g) * 16 + 2 * l) = (uint16_t)(q1 | q3 << 8);
+                if (l == 0) xsum[g] = sum;
             } else {
                 // elements 4l .. 4l+3 are bytes 4(l & 3) .. of chunk l >> 2
                 *reinterpret_cast<uint32_t *>(planes + ((l >> 2) * ng + g) * 16 + 4 * (l & 3)) =
@@ -100,9 +123,11 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
 
 // Quantizes a long v[0 .. n-1] (more groups of 32 than one pass of quantize_to_planes covers) into the same
 // planes: four threads per group, eight consecutive elements each, and two groups per thread at a time, so the
-// 152 groups of a 4,864-wide input take two passes instead of five. Same arithmetic as quantize_to_planes.
+// 152 groups of a 4,864-wide input take two passes instead of five. Same arithmetic as quantize_to_planes (and the
+// same group sums into xsum for int4 weights).
 template <int BITS, int FAM>
-__device__ __forceinline__ void quantize_to_planes_wide(const float *v, int n, uint8_t *planes, float *xs) {
+__device__ __forceinline__ void quantize_to_planes_wide(const float *v, int n, uint8_t *planes, float *xs,
+                                                        int *xsum) {
     constexpr int kPass = kThreads / 4;  // groups per pass and per slot
     const int ng = n / 32, l = threadIdx.x & 3;
     for (int base = 0; base < ng; base += 2 * kPass) {  // the same trip count in every thread (shuffles)
@@ -128,6 +153,7 @@ __device__ __forceinline__ void quantize_to_planes_wide(const float *v, int n, u
             m[h] = max(m[h], __shfl_xor_sync(0xffffffffu, m[h], 1));
             m[h] = max(m[h], __shfl_xor_sync(0xffffffffu, m[h], 2));
         }
+        int sum[2] = {0, 0};
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             if (g[h] >= ng) continue;
@@ -146,6 +172,8 @@ __device__ __forceinline__ void quantize_to_planes_wide(const float *v, int n, u
                 for (int i = 0; i < 8; i++) q[i] = (uint8_t)to_int8_x86(roundf(__fmul_rn(e[i], inv)));
             }
             if (BITS == 4) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) sum[h] += (int)(int8_t)q[i];
                 // elements 8l + 2i are even-plane bytes 4l + i; elements 8l + 2i + 1 odd-plane bytes 4l + i
                 *reinterpret_cast<uint32_t *>(planes + g[h] * 16 + 4 * l) = q[0] | q[2] << 8 | q[4] << 16 | q[6] << 24;
                 *reinterpret_cast<uint32_t *>(planes + (ng + g[h]) * 16 + 4 * l) =
@@ -157,6 +185,27 @@ __device__ __forceinline__ void quantize_to_planes_wide(const float *v, int n, u
             }
             if (l == 0) xs[g[h]] = scale;
         }
+        if (BITS == 4) {  // the groups' sums across their four threads (every thread takes part in the shuffles)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+                if (l == 0 && g[h] < ng) xsum[g[h]] = sum[h];
+            }
+        }
+    }
+}
+
+// The rmsnorm weights quantize_to_planes<..., NORM = true> applies in this thread: pass k's four elements of
+// group k * kThreads / (GS / 4) + threadIdx.x / (GS / 4). Read before the kernel waits for its producer.
+template <int GS>
+__device__ __forceinline__ void norm_weights_for_planes(const float *norm_w, int n, float4 (&nw4)[kNormPasses]) {
+    constexpr int TPG = GS / 4;
+    const int ng = n / GS, l = threadIdx.x % TPG;
+#pragma unroll
+    for (int k = 0; k < kNormPasses; k++) {
+        const int g = k * (kThreads / TPG) + threadIdx.x / TPG;
+        nw4[k] = g < ng ? __ldg(reinterpret_cast<const float4 *>(norm_w + GS * g) + l) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 }
 
@@ -339,14 +388,8 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         }
     }
     // the rmsnorm weights this thread applies (constants), also before the wait
-    float nw[kMaxNormPerThread];
-    if (PRO == kProNorm) {
-#pragma unroll
-        for (int i = 0; i < kMaxNormPerThread; i++) {
-            const int j = tid + i * kThreads;
-            nw[i] = j < n ? __ldg(p.norm_w + j) : 0.0f;
-        }
-    }
+    float4 nw4[kNormPasses];
+    if (PRO == kProNorm) norm_weights_for_planes<GS>(p.norm_w, n, nw4);
     if (EPI == kEpiStore) allow_consumer();
     wait_for_producer();
     // the residual's current value, loaded now so its latency overlaps the prologue
@@ -387,9 +430,8 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         float *xv = reinterpret_cast<float *>(smem + ((stage + 15) & ~(size_t)15));
         for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
         __syncthreads();
-        const float *qsrc = xv;
         if (PRO == kProNorm) {  // qwen.c:337-344, runq.c:394-407
-            float *xn = xv + n;
+            float *xn = xv + n;  // the squares
             __shared__ float s_inv;
             for (int j = tid; j < n; j += kThreads) xn[j] = __fmul_rn(xv[j], xv[j]);
             __syncthreads();
@@ -400,22 +442,19 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                 s_inv = __frcp_rn(__fsqrt_rn(ss));  // 1.0f / sqrtf(...): same value
             }
             __syncthreads();
-            const float sc = s_inv;
-#pragma unroll
-            for (int i = 0; i < kMaxNormPerThread; i++) {
-                const int j = tid + i * kThreads;
-                if (j < n) xn[j] = __fmul_rn(nw[i], __fmul_rn(sc, xv[j]));
-            }
-            __syncthreads();
-            qsrc = xn;
+            // normalized element by element inside the quantize (qwen.c:343's o[j] = w[j] * (ss * x[j]))
+            quantize_to_planes<BITS, FAM, GS, true>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s, nw4[0],
+                                                    nw4[1], s_inv);
+        } else if (GS == 32 && ng > kThreads / 8) {
+            quantize_to_planes_wide<BITS, FAM>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s);
+        } else {
+            const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            quantize_to_planes<BITS, FAM, GS, false>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s, z, z,
+                                                     0.0f);
         }
-        if (GS == 32 && ng > kThreads / 8)
-            quantize_to_planes_wide<BITS, FAM>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
-        else
-            quantize_to_planes<BITS, FAM, GS>(qsrc, n, reinterpret_cast<uint8_t *>(xplane), xs_s);
     }
     __syncthreads();
-    if (BITS == 4) {
+    if (BITS == 4 && PRO == kProQuantized) {  // the group sums (the quantizing prologues wrote them already)
         for (int g = tid; g < ng; g += kThreads) {
             const uint4 e = xplane[g], o = xplane[ng + g];
             int s = __dp4a((int)e.x, 0x01010101, 0);
