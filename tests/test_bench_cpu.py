@@ -75,3 +75,29 @@ def test_reference_sweep_line():
     (res,) = summary["results"]
     assert res["shape"] == "128x896 Q4" and res["us"] > 0 and res["GBps"] > 0
     assert res["bytes"] == 128 * 448 + 128 * 28 * 2 + 896 + 28 * 4 + 4 * 128
+
+
+@needs_ref
+def test_reference_arm_line_keeps_the_contract():
+    """`bench.py --impl reference` (the driver's reference arm): one JSON line with BASELINE.json's metric, the
+    reference's own qwen.c timed on the host cores, and its cpu_baseline / e2e objects."""
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "1"], capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    base = json.load(open(os.path.join(ROOT, "BASELINE.json")))
+    assert line["impl"] == "reference" and line["metric"] == base["metric"]
+    assert line["unit"] == "tok/s" and line["higher_is_better"] is True and line["value"] > 0
+    assert line["n_gpus"] == 1 and line["config"]["workload"]
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "reference" and cb["cores"] == os.cpu_count() and cb["value"] == line["value"] and cb["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun only rank 0 runs the reference arm; the other ranks exit 0 without work or output."""
+    env = dict(os.environ, RANK="1", LOCAL_RANK="1", WORLD_SIZE="2")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", "2"],
+                       capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
