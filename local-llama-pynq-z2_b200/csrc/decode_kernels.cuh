@@ -54,7 +54,9 @@ __device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinter
 // NORM: v is an rmsnorm's input and each element is first normalized as qwen.c:343 / runq.c:406 do,
 // fl(w * fl(sc * v)), with this thread's rmsnorm weights nw0 / nw1 (the four of its elements in the first /
 // second pass, see norm_weights_for_planes) and the inverse root sc; n is then at most kNormPasses passes of groups.
-template <int BITS, int FAM, int GS, bool NORM>
+// GSRC: v is the previous kernel's output in global memory, read with L2 loads (ld.global.cg: the lines may be
+// stale in this SM's L1), instead of a shared-memory copy.
+template <int BITS, int FAM, int GS, bool NORM, bool GSRC = false>
 __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs, int *xsum,
                                                    float4 nw0, float4 nw1, float sc) {
     constexpr int TPG = GS / 4;  // threads per group
@@ -65,7 +67,7 @@ __device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_
         const int g = base + threadIdx.x / TPG;
         const bool on = g < ng;
         float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (on) f = reinterpret_cast<const float4 *>(v + GS * g)[l];
+        if (on) f = GSRC ? ld_cg4(v + GS * g + 4 * l) : reinterpret_cast<const float4 *>(v + GS * g)[l];
         if (NORM) {
             const float4 w = pass == 0 ? nw0 : nw1;  // a select of registers, not an indexed local array
             f.x = __fmul_rn(w.x, __fmul_rn(sc, f.x));
@@ -428,12 +430,16 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         const size_t stage =
             (size_t)XP * ng * 16 + scale_bytes(ng) + (size_t)(EPI == kEpiSwiGLU ? 2 * p.rt : p.rt) * ps * 4;
         float *xv = reinterpret_cast<float *>(smem + ((stage + 15) & ~(size_t)15));
-        for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
-        __syncthreads();
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (PRO == kProNorm) {  // qwen.c:337-344, runq.c:394-407
-            float *xn = xv + n;  // the squares
+            float *xn = xv + n;  // the squares, written in the same pass that stages x
             __shared__ float s_inv;
-            for (int j = tid; j < n; j += kThreads) xn[j] = __fmul_rn(xv[j], xv[j]);
+            for (int j = tid; j < n / 4; j += kThreads) {
+                const float4 f = ld_cg4(p.src + 4 * j);
+                reinterpret_cast<float4 *>(xv)[j] = f;
+                reinterpret_cast<float4 *>(xn)[j] =
+                    make_float4(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y), __fmul_rn(f.z, f.z), __fmul_rn(f.w, f.w));
+            }
             __syncthreads();
             if (tid == 0) {
                 float ss = chain_sum(xn, n);
@@ -445,12 +451,18 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             // normalized element by element inside the quantize (qwen.c:343's o[j] = w[j] * (ss * x[j]))
             quantize_to_planes<BITS, FAM, GS, true>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s, nw4[0],
                                                     nw4[1], s_inv);
-        } else if (GS == 32 && ng > kThreads / 8) {
-            quantize_to_planes_wide<BITS, FAM>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s);
+        } else if (ng <= kThreads / (GS / 4)) {
+            // one pass of the quantize covers every group: each thread reads its own elements from L2, no staging
+            quantize_to_planes<BITS, FAM, GS, false, true>(p.src, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s,
+                                                           z, z, 0.0f);
         } else {
-            const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            quantize_to_planes<BITS, FAM, GS, false>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s, z, z,
-                                                     0.0f);
+            for (int j = tid; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(p.src + 4 * j);
+            __syncthreads();
+            if (GS == 32 && ng > kThreads / 8)
+                quantize_to_planes_wide<BITS, FAM>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s);
+            else
+                quantize_to_planes<BITS, FAM, GS, false>(xv, n, reinterpret_cast<uint8_t *>(xplane), xs_s, xsum_s, z,
+                                                         z, 0.0f);
         }
     }
     __syncthreads();
