@@ -10,14 +10,27 @@ greedy decode. One step = 128 greedy tokens from the filled prompt cache (positi
   e2e        the same metric through the public C ABI with host buffers: per step mvb_qwen_rewind (state copied
              from pinned host memory) and mvb_qwen_decode (128 ids copied back to host memory), host wall clock.
   roofline   the dominant matvec kernel kind of the step (the path's kernel; every kind, attention included, is
-             listed in per_kind with its share), from CUDA events around every kernel of one instrumented step at
-             the middle decode position (position 191), against MEASURED_PEAKS.json's HBM bandwidth.
+             listed in per_kind with its share). Times come from the step exactly as the graph runs it (programmatic
+             dependent launch included), every kernel stamping the GPU's global timer (mvb_qwen_stamps): a kernel's
+             time is its last CTA's end minus the previous kernel's, so the kinds partition the step. Median of 5
+             steps at the middle decode position (position 191), against MEASURED_PEAKS.json's HBM bandwidth.
+             `traffic` is the DRAM bytes per launch of an ncu capture (profiles/traffic_per_launch.txt), given only
+             when that capture was taken on the kernel sources of this tree (their hash is stamped in the file).
   cpu_baseline  the reference's own CPU build (oracle/_ref/qwen, -O3 -fopenmp -ffp-contract=off) on the same
-             file and prompt, all host cores, its own "generated tok/s".
+             file and prompt, all host cores, its own "generated tok/s": median of K runs (the same count as the
+             reference arm's steps).
+  dropin     the reference's unchanged qwen.c linked against this library (oracle/_ref/qwen_b200: 200 synchronous
+             fpga_matvec4 calls per token through the drop-in C ABI), same file and prompt, its own "generated tok/s",
+             plus the library's per-call breakdown of fpga_matvec4 (MATVEC_STATS=1 run).
+  sharded    config 5 (row-sharded 131072x8192 Q4 and the 151936-row Q8 head, batch 1 and 32) over all N ranks with
+             the all-gather fused into the kernel (mvb_gather_*), beside the plain matvec + NCCL all-gather, each
+             gathered vector checked bit for bit against the unsharded matvec (or matmul) of the whole matrix.
 Every decode step reads the 263.7 MB of weights of a token, more than the 126 MB L2, so no flush is needed.
 
---impl reference times the reference's CPU implementation (oracle/_ref/qwen) on the same workload.
-Multi-GPU (torchrun): the 0.5B decode does not shard; every rank runs an independent replica (weak scaling).
+--impl reference times the reference's CPU implementation (oracle/_ref/qwen) on the same workload: K runs after
+W warm-up runs, each one qwen.c generation of 128 greedy tokens from the 128-token prompt.
+Multi-GPU (torchrun): the 0.5B decode does not shard; every rank runs an independent replica (weak scaling), and
+the sharded block measures the one collective of the design.
 """
 import argparse
 import importlib.util
@@ -33,6 +46,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "local-llama-pynq-z2_b200")
 REF_QWEN = os.path.join(ROOT, "oracle", "_ref", "qwen")
+REF_QWEN_B200 = os.path.join(ROOT, "oracle", "_ref", "qwen_b200")
 DATA = os.environ.get("MVB_DATA", "/tmp/mvb_data")
 METRIC = "Q4_0 decode tok/s (Qwen2.5-0.5B arch, 1 B200); matvec HBM GB/s vs peak"
 PROMPT_LEN, GEN = 128, 128
@@ -40,6 +54,26 @@ PUBLISHED_TOKS = 3.7  # reference README: Qwen2.5-Coder-0.5B Q4_0 decode, FPGA m
 WORKLOAD = ("qwen2.5-0.5b-arch Q4_0 decode (config 3): synthetic seeded .qwb (Q4 layers, Q8 65536-row head), "
             "128-token prompt then 128 greedy tokens per step")
 MATVEC_KINDS = ("qkv", "o_proj", "gate_up", "down", "head")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
+
+
+def kernel_sources_sha():
+    """Short hash of the library's kernel sources (csrc/*.cu, *.cuh, *.h): names the code an ncu capture covers."""
+    import glob
+    import hashlib
+    h = hashlib.sha256()
+    for f in sorted(glob.glob(os.path.join(PKG, "csrc", "*"))):
+        if f.endswith((".cu", ".cuh", ".h")):
+            h.update(os.path.basename(f).encode())
+            h.update(open(f, "rb").read())
+    return h.hexdigest()[:12]
+
+
+def decode_config(world):
+    """The `config` object of both arms' decode lines (the same workload and keys)."""
+    return {"workload": WORKLOAD, "prompt_tokens": PROMPT_LEN, "gen_tokens_per_step": GEN, "replicas": world,
+            "l2": "no flush: each token reads 263.7 MB of weights > 126 MB L2",
+            "baseline": "3.7 tok/s, reference README.md:36 (PYNQ-Z2 FPGA)"}
 
 
 def load_pkg():
@@ -96,16 +130,33 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def run_reference_qwen(model, prompt, n_gen, threads):
-    env = dict(os.environ, OMP_NUM_THREADS=str(threads))
-    r = subprocess.run([REF_QWEN, model, "--ids", ",".join(map(str, prompt)), "-t", "0", "-n", str(n_gen), "-c", "512"],
+def run_reference_qwen(model, prompt, n_gen, threads, binary=REF_QWEN, env_extra=None):
+    """One qwen.c run (`binary`: the CPU build, or qwen_b200, the same source linked against this library) with
+    --ids and greedy sampling: (its generated tok/s, tokens, prompt seconds, ids, stderr)."""
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads), **(env_extra or {}))
+    r = subprocess.run([binary, model, "--ids", ",".join(map(str, prompt)), "-t", "0", "-n", str(n_gen), "-c", "512"],
                        capture_output=True, text=True, env=env, timeout=900)
     if r.returncode != 0:
-        raise RuntimeError("reference qwen failed: " + r.stderr[-500:])
+        raise RuntimeError(os.path.basename(binary) + " failed: " + r.stderr[-500:])
     m = re.search(r"generated: (\d+) tokens, ([\d.]+) tok/s", r.stderr)
     pm = re.search(r"prompt: (\d+) tokens in ([\d.]+) s", r.stderr)
     ids = [int(t) for t in r.stdout.strip().split(",") if t]
-    return float(m.group(2)), int(m.group(1)), float(pm.group(2)), ids
+    return float(m.group(2)), int(m.group(1)), float(pm.group(2)), ids, r.stderr
+
+
+def reference_runs(path, prompt, runs, warmup, threads):
+    """qwen.c's CPU build, `warmup` untimed runs then `runs` runs: (median generated tok/s, runs, last ids, last
+    prompt seconds). The reference arm and the decode line's cpu_baseline both use this, with the same count."""
+    for _ in range(warmup):
+        run_reference_qwen(path, prompt, GEN, threads)
+    res = [run_reference_qwen(path, prompt, GEN, threads) for _ in range(runs)]
+    return statistics.median(r[0] for r in res), len(res), res[-1][3], res[-1][2]
+
+
+def reference_sample(threads, runs):
+    return (f"qwen.c CPU build (-O3 -fopenmp -ffp-contract=off, OMP_NUM_THREADS={threads}) on the same .qwb and "
+            f"128-token prompt, {runs} runs of 128 greedy tokens; value = median of its own 'generated tok/s' (prompt "
+            f"time excluded, as in the reference's report)")
 
 
 def model_path(rank, world):
@@ -131,59 +182,93 @@ def reference_arm(args, rank, world):
     path = model_path(0, 1)
     threads = os.cpu_count()
     prompt = prompt_ids()
-    run_reference_qwen(path, prompt, 4, threads)  # warm-up: pages the file in
-    runs = [run_reference_qwen(path, prompt, GEN, threads) for _ in range(min(args.steps, 3))]
-    value = statistics.median(r[0] for r in runs)
-    sample = (f"qwen.c CPU build (-O3 -fopenmp -ffp-contract=off, OMP_NUM_THREADS={threads}) on the same .qwb and "
-              f"128-token prompt, {len(runs)} runs of 128 greedy tokens; value = median of its own 'generated tok/s' "
-              f"(prompt time excluded, as in the reference's report)")
+    value, runs, _, _ = reference_runs(path, prompt, args.steps, max(1, args.warmup), threads)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
-            "steps": len(runs), "warmup": 1, "ms_per_step": round(1000.0 * GEN / value, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": round(value / PUBLISHED_TOKS, 3), "dtype": "int4/int8->int32, fp32",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT_LEN, "gen_tokens": GEN},
+            "steps": runs, "warmup": max(1, args.warmup), "ms_per_step": round(1000.0 * GEN / value, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / PUBLISHED_TOKS, 3),
+            "dtype": "int4/int8->int32, fp32", "data": "synthetic", "config": decode_config(world),
             "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                             "sample": sample},
+                             "sample": reference_sample(threads, runs)},
             "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+def read_traffic(kind):
+    """DRAM bytes (read + write) per launch of decode kernel `kind` from the committed ncu summary, with where it
+    came from; None when the file's capture was taken on kernel sources other than this tree's."""
+    sha_now = kernel_sources_sha()
+    if not os.path.exists(TRAFFIC_FILE):
+        return None, "no capture"
+    sha_file, value = None, None
+    for line in open(TRAFFIC_FILE):
+        parts = line.split()
+        if len(parts) == 2 and parts[0] == "sources":
+            sha_file = parts[1]
+        elif len(parts) == 2 and parts[0] == kind:
+            value = float(parts[1])
+    src = f"profiles/traffic_per_launch.txt (ncu capture of kernel sources {sha_file}; this tree {sha_now})"
+    if sha_file != sha_now:
+        return None, src + ": not this tree's kernels, so not used"
+    return value, src
+
+
 def step_roofline(dec, token, pos, reps=5):
-    """Per-kernel-kind device times of the decode step at (token, pos), from CUDA events around every kernel of the
-    instrumented step (mvb_qwen_profile, mean of `reps`), against the measured HBM peak: the algorithmic GB/s of
-    the dominant matvec kind (the path's kernel, decode_matvec_kernel) and of all matvecs together. Every kind,
-    attention included, is in per_kind with its share of the step."""
+    """Where the decode step's time goes, kernel kind by kernel kind, as the captured graph runs it: `reps` steps at
+    (token, pos) with every kernel stamping the global timer (mvb_qwen_stamps). A kernel's time is its last CTA's
+    end minus the previous kernel's (so the kinds partition the step, the kernel boundaries included); its
+    in-kernel time starts when its first CTA got past the wait for the previous kernel. The roofline is the
+    algorithmic GB/s of the dominant matvec kind (the path's kernel, decode_matvec_kernel) and of all matvecs
+    together, against the measured HBM peak. The isolated per-kernel times (CUDA events around every kernel, no
+    overlap, mvb_qwen_profile) are given beside them."""
     import numpy as np
     info = dec.kernel_info(pos)
-    runs = []
+    seg_runs, inside_runs, iso_runs = [], [], []
     for _ in range(reps):
         dec.rewind(token, pos, -1)
-        runs.append(dec.profile())
-    ms = np.mean(runs, axis=0)
+        st = dec.stamps()
+        ends = st[:, 1]
+        seg_runs.append(np.diff(np.concatenate([[0.0], ends])))
+        inside_runs.append(st[:, 1] - st[:, 0])
+        dec.rewind(token, pos, -1)
+        iso_runs.append(dec.profile() * 1000.0)
+    seg = np.median(seg_runs, axis=0)
+    inside = np.median(inside_runs, axis=0)
+    iso = np.median(iso_runs, axis=0)
     kinds = {}
-    for (kind, layer, b), t in zip(info, ms):
-        k = kinds.setdefault(kind, {"launches": 0, "ms": 0.0, "bytes": 0.0})
+    for (kind, layer, b), t, ti, tiso in zip(info, seg, inside, iso):
+        k = kinds.setdefault(kind, {"launches": 0, "us": 0.0, "inside": 0.0, "iso": 0.0, "bytes": 0.0})
         k["launches"] += 1
-        k["ms"] += float(t)
+        k["us"] += float(t)
+        k["inside"] += float(ti)
+        k["iso"] += float(tiso)
         k["bytes"] += b
-    step_ms = float(ms.sum())
-    dom = max((k for k in kinds if k in MATVEC_KINDS), key=lambda k: kinds[k]["ms"])
+    step_us = float(seg.sum())
+    dom = max((k for k in kinds if k in MATVEC_KINDS), key=lambda k: kinds[k]["us"])
     peak, peak_kind = peaks()
     d = kinds[dom]
-    achieved = d["bytes"] / (d["ms"] / 1000.0) / 1e9
-    mv_bytes = sum(kinds[k]["bytes"] for k in MATVEC_KINDS)
-    mv_ms = sum(kinds[k]["ms"] for k in MATVEC_KINDS)
-    return {"bound": "hbm", "kernel": f"decode_matvec_kernel ({dom})", "kind": dom, "achieved": round(achieved, 1), "peak": peak,
-            "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-            "traffic": None, "bytes_per_launch": round(d["bytes"] / d["launches"]),
-            "us_per_launch": round(1000.0 * d["ms"] / d["launches"], 3),
-            "step_share": round(d["ms"] / step_ms, 4),
-            "all_matvecs": {"bytes_per_token": round(mv_bytes), "ms_per_token": round(mv_ms, 4),
-                            "achieved": round(mv_bytes / (mv_ms / 1000.0) / 1e9, 1),
-                            "frac": round(mv_bytes / (mv_ms / 1000.0) / 1e9 / peak, 4)},
-            "instrumented_step_ms": round(step_ms, 4),
-            "per_kind": {k: {"launches": v["launches"], "us_per_launch": round(1000 * v["ms"] / v["launches"], 2),
-                             "GBps": round(v["bytes"] / (v["ms"] / 1000) / 1e9, 1),
-                             "step_share": round(v["ms"] / step_ms, 4)} for k, v in kinds.items()}}
+    achieved = d["bytes"] / (d["us"] * 1e-6) / 1e9
+    mv_bytes = sum(kinds[k]["bytes"] for k in MATVEC_KINDS if k in kinds)
+    mv_us = sum(kinds[k]["us"] for k in MATVEC_KINDS if k in kinds)
+    all_bytes = sum(k["bytes"] for k in kinds.values())
+    traffic, traffic_src = read_traffic(dom)
+    return {"bound": "hbm", "kernel": f"decode_matvec_kernel ({dom})", "kind": dom, "achieved": round(achieved, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+            "traffic": traffic, "traffic_source": traffic_src, "bytes_per_launch": round(d["bytes"] / d["launches"]),
+            "us_per_launch": round(d["us"] / d["launches"], 3), "step_share": round(d["us"] / step_us, 4),
+            "timing": "in the step graph with programmatic launch (mvb_qwen_stamps, %globaltimer): a kernel's time = "
+                      "its last CTA's end minus the previous kernel's; median of 5 steps at position " + str(pos),
+            "stamped_step_us": round(step_us, 2),
+            "all_matvecs": {"bytes_per_token": round(mv_bytes), "us_per_token": round(mv_us, 2),
+                            "achieved": round(mv_bytes / (mv_us * 1e-6) / 1e9, 1),
+                            "frac": round(mv_bytes / (mv_us * 1e-6) / 1e9 / peak, 4)},
+            "whole_step": {"bytes_per_token": round(all_bytes), "achieved": round(all_bytes / (step_us * 1e-6) / 1e9, 1),
+                           "frac": round(all_bytes / (step_us * 1e-6) / 1e9 / peak, 4)},
+            "isolated_step_us": round(float(iso.sum()), 2),
+            "per_kind": {k: {"launches": v["launches"], "us_per_launch": round(v["us"] / v["launches"], 3),
+                             "in_kernel_us": round(v["inside"] / v["launches"], 3),
+                             "isolated_us": round(v["iso"] / v["launches"], 3),
+                             "GBps": round(v["bytes"] / (v["us"] * 1e-6) / 1e9, 1),
+                             "step_share": round(v["us"] / step_us, 4)} for k, v in kinds.items()}}
 
 
 def our_arm(args, rank, world, local_rank):
@@ -251,13 +336,6 @@ def our_arm(args, rank, world, local_rank):
     # roofline: one instrumented step at the middle decode position, 5 repeats
     mid = pos0 + GEN // 2
     roofline = step_roofline(dec, tok0 if mid == pos0 else int(ids_first[mid - pos0 - 1]), mid)
-    dom = roofline["kind"]
-    traffic = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
-    if os.path.exists(traffic):
-        for line in open(traffic):
-            parts = line.split()
-            if len(parts) == 2 and parts[0] == dom:
-                roofline["traffic"] = float(parts[1])
     # prompt prefill through the public API (host wall clock, the call returns when the cache is written): the
     # batched path (tensor-core matmuls) and one decode step per fed token
     def timed_prefill(fn, reps=3):
@@ -275,29 +353,49 @@ def our_arm(args, rank, world, local_rank):
                "tokenwise_tok_s": round((PROMPT_LEN - 1) / t_pf_tok, 1),
                "how": "mvb_qwen_prefill (batched: tensor-core matmuls) and mvb_qwen_prefill_tokenwise (one decode "
                       "step per token); host wall clock of the synchronous call, median of 3"}
-    cpu = None
+    dec.close()
+    cpu, dropin = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and os.path.exists(REF_QWEN):
         threads = os.cpu_count()
-        tps, n, ref_prompt_s, ref_ids = run_reference_qwen(path, prompt, GEN, threads)
+        tps, runs, ref_ids, ref_prompt_s = reference_runs(path, prompt, args.steps, 1, threads)
         cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-               "sample": f"qwen.c CPU build (-O3 -fopenmp -ffp-contract=off) on the same .qwb and prompt, one run of "
-                         f"{n} greedy tokens, its own generated tok/s",
-               "same_ids_as_b200": ref_ids == ids_first.tolist()}
+               "sample": reference_sample(threads, runs), "same_ids_as_b200": ref_ids == ids_first.tolist()}
         prefill["reference_prompt_s"] = ref_prompt_s
-    dec.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and os.path.exists(REF_QWEN_B200):
+        dropin = dropin_block(path, prompt, ids_first.tolist(), local_rank)
+    sharded = None
+    if not args.no_sharded:
+        sharded = sharded_cases(rank, world, max(args.steps, 50), max(args.warmup, 3), dist)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(1000.0 * t_dev / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": round(value / PUBLISHED_TOKS, 2),
-                "dtype": "int4/int8->int32, fp32", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT_LEN, "gen_tokens_per_step": GEN,
-                           "replicas": world, "l2": "no flush: each token reads 263.7 MB of weights > 126 MB L2",
-                           "baseline": "3.7 tok/s, reference README.md:36 (PYNQ-Z2 FPGA)"},
+                "dtype": "int4/int8->int32, fp32", "data": "synthetic", "config": decode_config(world),
                 "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 32,
                         "d2h_bytes_per_step": 4 * GEN + 32},
-                "gpu_launches": args.steps * GEN * cfg["kernels_per_step"], "clocks": clk, "prefill": prefill}
+                "gpu_launches": args.steps * GEN * cfg["kernels_per_step"], "clocks": clk, "prefill": prefill,
+                "dropin": dropin, "sharded": sharded}
         print(json.dumps(line), flush=True)
+
+
+def dropin_block(path, prompt, ids_b200, gpu):
+    """The drop-in boundary as the reference's users would run it: qwen.c unchanged, compiled with -DFPGA against
+    include/matvec_fpga.h and linked to this library (oracle/_ref/qwen_b200), on the same file and prompt: each
+    matvec is one synchronous fpga_matvec4 call (200 per token) with host buffers. Median of 3 runs of its own
+    'generated tok/s'; then one run with MATVEC_STATS=1, whose fpga_close() reports the per-call breakdown."""
+    threads = os.cpu_count()
+    env = {"FPGA_MEMIDX": str(gpu)}
+    runs = [run_reference_qwen(path, prompt, GEN, threads, REF_QWEN_B200, env) for _ in range(3)]
+    _, _, _, _, err = run_reference_qwen(path, prompt, GEN, threads, REF_QWEN_B200, dict(env, MATVEC_STATS="1"))
+    stats = None
+    m = re.search(r"matvec stats: (\{.*\})", err)
+    if m:
+        stats = json.loads(m.group(1))
+    return {"value": round(statistics.median(r[0] for r in runs), 2), "unit": "tok/s", "runs": len(runs),
+            "how": "qwen.c unchanged, -DFPGA, linked to libmatvec_b200.so (oracle/_ref/qwen_b200); its own "
+                   "'generated tok/s' (prompt excluded); 200 synchronous fpga_matvec4 calls per token",
+            "same_ids_as_b200": runs[-1][3] == ids_b200, "per_call": stats}
 
 
 # ---- isolated-kernel modes (not the driver's default line) ----
@@ -584,130 +682,152 @@ def step_mode(args):
                       "warmup": args.warmup}))
 
 
-def sharded_mode(args, rank, world, local_rank):
-    """Config 5: one matrix row-sharded across the ranks (contiguous row blocks), each rank's matvec on its
-    shard, and every rank ends the step holding the whole fp32 output. Two ways are timed per step with CUDA
-    events, max over ranks: the library's fused kernel that stores its rows into every rank's output over NVLink
-    (mvb_gather_matvec4, the reported number), and the plain matvec followed by an NCCL all-gather (with the
-    all-gather alone timed too). Both must produce the same gathered vector, bit for bit."""
+SHARDED_CASES = ((8192, 131072, 4), (896, 151936, 8))  # config 5: (n columns, d rows, weight bits)
+
+
+def sharded_cases(rank, world, iters, warmup, dist):
+    """Config 5 on `world` ranks (one per GPU; dist is torch.distributed, or None for one rank): each matrix
+    row-sharded in contiguous blocks (rows per rank = ceil(d / world), the last block padded), every rank ending the
+    step with the whole fp32 output. Timed per step with CUDA events, max over ranks: the fused kernel that stores its
+    rows into every rank's output over NVLink (mvb_gather_matvec4 at batch 1, mvb_gather_gemm4 at batch 32: the
+    reported number), the plain matvec/matmul of the shard alone, and (world > 1) the plain call followed by an NCCL
+    all-gather, with the all-gather alone. Every rank checks its gathered output bit for bit against the unsharded
+    matvec (or matmul) of the whole matrix, and the NCCL path's result against the fused one."""
     import torch
-    import torch.distributed as dist
-    mvb = load_pkg()
-    torch.cuda.set_device(local_rank)
-    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    mvb = sys.modules.get("mvb") or load_pkg()
     peak, peak_kind = peaks()
     results = []
-    for n, d, bits in ((8192, 131072, 4), (896, 151936, 8)):
-        rows = -(-d // world)  # rows per rank (the last rank's block is padded with unused rows)
-        r0 = rank * rows
-        mine = max(0, min(rows, d - r0))
-        b_local = _alg_bytes(n, rows, bits)
-        copies = max(1, -(-300 * 2**20 // b_local))
-        w, sc = _rand_matrix(torch, n, rows, bits, copies, gen)
-        xq = torch.randint(-127, 128, (n,), dtype=torch.int8, device="cuda",
-                           generator=torch.Generator(device="cuda").manual_seed(7))
-        xs = torch.full((n // 32,), 0.01, device="cuda")
-        part = torch.empty(rows, device="cuda")
-        full = torch.empty(rows * world, device="cuda")
 
-        def step(i):
-            mvb.matvec4(w[i % copies], sc[i % copies], xq, xs, part, n, rows, bits)
-            dist.all_gather_into_tensor(full, part)
-
-        def gather_only(i):
-            dist.all_gather_into_tensor(full, part)
-
-        def timed(fn, k):
-            for i in range(args.warmup):
-                fn(i)
-            torch.cuda.synchronize()
+    def sync():
+        torch.cuda.synchronize()
+        if dist:
             dist.barrier()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(k):
-                fn(i)
-            e1.record()
-            torch.cuda.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / 1000.0 / k], dtype=torch.float64, device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            return float(t.item())
+        torch.cuda.synchronize()
 
-        t_step = timed(step, args.steps)
-        t_ag = timed(gather_only, args.steps)
-        # correctness: this rank's block of the gathered output equals its local result
-        ok = torch.equal(full[r0:r0 + rows], part)
+    def timed(fn):
+        for i in range(warmup):
+            fn(i)
+        sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(iters):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1000.0 / iters
+        if dist:
+            tt = torch.tensor([t], dtype=torch.float64, device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
 
-        # the same step with the all-gather fused into the matvec kernel (peer stores over NVLink)
-        g = mvb.ShardGather(rank, world, rows)
+    def all_ranks(ok):
+        if not dist:
+            return bool(ok)
+        t = torch.tensor([1 if ok else 0], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return bool(t.item())
+
+    def shard(q, rows, n, bits):
+        """Rank q's block of copy 0 of the matrix (seeded by q): the same bytes on every rank."""
+        g0 = torch.Generator(device="cuda").manual_seed(1000 + q)
+        w, sc = _rand_matrix(torch, n, rows, bits, 1, g0)
+        return w[0], sc[0]
+
+    def connect(g):
         handles = [None] * world
-        dist.all_gather_object(handles, g.handle())
+        if dist:
+            dist.all_gather_object(handles, g.handle())
+        else:
+            handles = [g.handle()]
         g.connect(handles)
 
-        def fused(i):
-            g.matvec4(w[i % copies], sc[i % copies], xq, xs, n, bits)
-
-        t_fused = timed(fused, args.steps)
-        step(0)
-        fused(0)
-        ok = ok and torch.equal(g.output(), full) and g.error() == 0
-        okt = torch.tensor([1 if ok else 0], device="cuda")
-        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
-        torch.cuda.synchronize()
-        dist.barrier()  # no rank's kernel still stores into a buffer about to be freed
-        g.close()
-        dist.barrier()
+    for n, d, bits in SHARDED_CASES:
+        rows = -(-d // world)
         total = _alg_bytes(n, d, bits)
-        results.append({"shape": f"{d}x{n} Q{bits}", "batch": 1, "n_gpus": world, "rows_per_gpu": rows,
-                        "us_per_step": round(t_fused * 1e6, 2),
-                        "GBps_total": round(total / t_fused / 1e9, 1),
-                        "frac_of_aggregate_hbm": round(total / t_fused / 1e9 / (peak * world), 4),
-                        "nccl_us_per_step": round(t_step * 1e6, 2), "nccl_allgather_us": round(t_ag * 1e6, 2),
-                        "gathered_ok": bool(okt.item())})
-        # batch 32: the tensor-core matmul on each rank's shard; rows gathered by its epilogue (fused) or by an
-        # NCCL all-gather of each rank's [32 x rows] block after a plain matmul
+        b_local = _alg_bytes(n, rows, bits)
+        copies = max(1, -(-300 * 2**20 // b_local))  # this rank's copies rotate past the 126 MB L2
+        w0, s0 = shard(rank, rows, n, bits)
+        w_more, s_more = _rand_matrix(torch, n, rows, bits, copies - 1,
+                                      torch.Generator(device="cuda").manual_seed(1234 + rank)) if copies > 1 else ([], [])
+        w, sc = [w0] + w_more, [s0] + s_more
+        xq = torch.randint(-127, 128, (n,), dtype=torch.int8, device="cuda",
+                           generator=torch.Generator(device="cuda").manual_seed(7))
+        xs = torch.rand(n // 32, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9)) * 0.05
         m = 32
         xq32 = torch.randint(-127, 128, (m, n), dtype=torch.int8, device="cuda",
                              generator=torch.Generator(device="cuda").manual_seed(8))
-        xs32 = torch.full((n // 32, m), 0.01, device="cuda")
-        gb = mvb.ShardGather(rank, world, rows, tokens=m)
-        handles = [None] * world
-        dist.all_gather_object(handles, gb.handle())
-        gb.connect(handles)
-        blk = torch.empty((m, rows), device="cuda")
-        blocks = torch.empty((world, m, rows), device="cuda")
-
-        def fused32(i):
-            gb.gemm4(w[i % copies], sc[i % copies], xq32, xs32, n, m, m, bits)
-
-        def nccl32(i):
-            mvb.gemm4(w[i % copies], sc[i % copies], xq32, xs32, blk, n, rows, m, m, bits)
-            dist.all_gather_into_tensor(blocks, blk)
-
-        t_f32 = timed(fused32, args.steps)
-        t_n32 = timed(nccl32, args.steps)
-        fused32(0)
-        nccl32(0)
+        xs32 = torch.rand((n // 32, m), device="cuda", generator=torch.Generator(device="cuda").manual_seed(10)) * 0.05
+        # the unsharded results of the whole (padded) matrix, from every rank's copy-0 block
+        blocks = [shard(q, rows, n, bits) for q in range(world)]
+        w_full = torch.cat([b[0] for b in blocks])
+        s_full = torch.cat([b[1] for b in blocks])
+        del blocks
+        ref1 = torch.empty(rows * world, device="cuda")
+        mvb.matvec4(w_full, s_full, xq, xs, ref1, n, rows * world, bits)
+        ref32 = torch.empty((m, rows * world), device="cuda")
+        mvb.gemm4(w_full, s_full, xq32, xs32, ref32, n, rows * world, m, m, bits)
         torch.cuda.synchronize()
-        ok32 = torch.equal(gb.output(), blocks.permute(1, 0, 2).reshape(m, world * rows)) and gb.error() == 0
-        okt = torch.tensor([1 if ok32 else 0], device="cuda")
-        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
-        torch.cuda.synchronize()
-        dist.barrier()
-        gb.close()
-        dist.barrier()
-        results.append({"shape": f"{d}x{n} Q{bits}", "batch": m, "n_gpus": world, "rows_per_gpu": rows,
-                        "us_per_step": round(t_f32 * 1e6, 2), "GBps_total": round(total / t_f32 / 1e9, 1),
-                        "frac_of_aggregate_hbm": round(total / t_f32 / 1e9 / (peak * world), 4),
-                        "tokens_per_s": round(m / t_f32, 1), "nccl_us_per_step": round(t_n32 * 1e6, 2),
-                        "gathered_ok": bool(okt.item())})
+        if mvb.gemm_status() != 0:
+            raise RuntimeError("sharded: a matmul wait gave up")
+        del w_full, s_full
+        torch.cuda.empty_cache()
+        for batch in (1, m):
+            g = mvb.ShardGather(rank, world, rows, tokens=batch)
+            connect(g)
+            part = torch.empty((batch, rows), device="cuda")
+            if batch == 1:
+                fused = lambda i: g.matvec4(w[i % copies], sc[i % copies], xq, xs, n, bits)
+                plain = lambda i: mvb.matvec4(w[i % copies], sc[i % copies], xq, xs, part, n, rows, bits)
+            else:
+                fused = lambda i: g.gemm4(w[i % copies], sc[i % copies], xq32, xs32, n, m, m, bits)
+                plain = lambda i: mvb.gemm4(w[i % copies], sc[i % copies], xq32, xs32, part, n, rows, m, m, bits)
+            t_fused = timed(fused)
+            t_plain = timed(plain)
+            fused(0)
+            torch.cuda.synchronize()
+            got = g.output().clone()
+            ref = ref1 if batch == 1 else ref32
+            same = bool(torch.equal(got.view(torch.int32), ref.view(torch.int32))) and g.error() == 0
+            line = {"shape": f"{d}x{n} Q{bits}", "batch": batch, "n_gpus": world, "rows_per_gpu": rows,
+                    "us_per_step": round(t_fused * 1e6, 2), "GBps_total": round(total / t_fused / 1e9, 1),
+                    "frac_of_aggregate_hbm": round(total / t_fused / 1e9 / (peak * world), 4),
+                    "shard_alone_us": round(t_plain * 1e6, 2)}
+            if batch > 1:
+                line["tokens_per_s"] = round(batch / t_fused, 1)
+            if dist and world > 1:
+                full = torch.empty((world, batch, rows), device="cuda")
+                ag = lambda i: dist.all_gather_into_tensor(full, part)
+                nccl = lambda i: (plain(i), ag(i))
+                line["nccl_path_us"] = round(timed(nccl) * 1e6, 2)
+                line["nccl_allgather_us"] = round(timed(ag) * 1e6, 2)
+                nccl(0)
+                torch.cuda.synchronize()
+                same = same and bool(torch.equal(full.permute(1, 0, 2).reshape(batch, world * rows).view(torch.int32),
+                                                 got.view(batch, -1).view(torch.int32)))
+            line["bit_identical"] = all_ranks(same)
+            sync()  # no rank's kernel still stores into a buffer about to be freed
+            g.close()
+            sync()
+            results.append(line)
         del w, sc
         torch.cuda.empty_cache()
+    return {"collective": "fused peer stores over NVLink (mvb_gather_matvec4 at batch 1, mvb_gather_gemm4 at batch 32, "
+                          "the reported us_per_step); NCCL all_gather_into_tensor after the plain call for comparison",
+            "check": "every rank's gathered output equals the unsharded matvec/matmul of the whole matrix bit for bit "
+                     "(and the NCCL path's)", "peak_per_gpu": peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "iters": iters, "results": results}
+
+
+def sharded_mode(args, rank, world, local_rank):
+    """Config 5 alone (the sharded block of the decode line): prints its results on rank 0."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    load_pkg()
+    out = sharded_cases(rank, world, max(args.steps, 50), max(args.warmup, 3), dist if world > 1 else None)
     if rank == 0:
-        print(json.dumps({"mode": "sharded", "peak_per_gpu": peak, "peak_source": f"{peak_kind} hbm_gbs",
-                          "collective": "fused peer stores (mvb_gather_matvec4 at batch 1, mvb_gather_gemm4 at "
-                                        "batch 32); NCCL all_gather_into_tensor for comparison",
-                          "results": results}), flush=True)
+        print(json.dumps({"mode": "sharded", **out}), flush=True)
 
 
 RUNQ_MODELS = {"stories15m": ("STORIES15M", "stories15M"), "stories110m": ("STORIES110M", "stories110M")}
@@ -857,6 +977,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true", help="decode: leave out the sharded (config 5) block")
     ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
     ap.add_argument("--model", default="", choices=["", *RUNQ_MODELS], help="runq: only this model")

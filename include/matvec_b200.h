@@ -124,6 +124,13 @@ int mvb_qwen_rewind(void *model, int token, int pos, int n_prompt);
  * writing each kernel's duration in ms to ms[0 .. count-1] (cap >= kernels per step). Returns the count or -1. */
 int mvb_qwen_profile(void *model, float *ms, int cap);
 
+/* Runs one step exactly as the captured graph runs it (programmatic dependent launch, no events between kernels),
+ * with every kernel stamping the GPU's global timer: us[2k] = when kernel k's first CTA got past its wait for
+ * kernel k - 1, us[2k + 1] = when its last CTA finished, in microseconds after the step's first kernel started
+ * (cap >= 2 * kernels per step). us[2k + 1] - us[2k - 1] is kernel k's share of the step's critical path. The
+ * state advances like a normal step. Returns the kernel count, or -1. */
+int mvb_qwen_stamps(void *model, double *us, int cap);
+
 /* Kernel k of the step: its kind ("embed", "qkv", "attention", "o_proj", "gate_up", "down", "final_norm",
  * "head", "next_token") into kind[kind_len], its layer (-1 outside the layers), and the bytes it must move at
  * position pos (weights, scales, activations, KV-cache rows). 0, or -1. */
@@ -147,17 +154,20 @@ void mvb_qwen_free(void *model);
  * latency-critical path where cudaMalloc's implicit device-wide synchronization would stall other work, and code
  * inside a framework that owns the device allocator. Its scratch (the quantized activations) is a fixed device
  * array of 2,304 bytes that every GPU using the library holds until the process exits, so n is at most 2048
- * (larger n returns -1 with a message). The first call on each device looks up that array's address; make that
- * first call before any stream capture. Every call overwrites the whole scratch it reads, so nothing has to be
- * cleared between calls, but all calls on a device share the one array: calls that can run at the same time on
- * one GPU (for example on two streams) race. Returns 0, or -1 with the reason in mvb_last_error(). */
+ * (larger n returns -1 with a message). The first call on each device looks up that array's address (again after
+ * a cudaDeviceReset, whose next context holds a new copy of the array); make that first call before any stream
+ * capture. Every pointer is checked (null; w 16-byte, ws 2-byte, x, norm_w and out 4-byte aligned) before anything
+ * is launched, so a refused call changes nothing on the device. Every call overwrites the whole scratch it reads,
+ * so nothing has to be cleared between calls, but all calls on a device share the one array: calls that can run
+ * at the same time on one GPU (for example on two streams) race. Returns 0, or -1 with the reason in
+ * mvb_last_error(). */
 int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, const void *w, const void *ws, float *out,
                             int n, int d, int wbits, void *stream);
 
 /* The decode's expf on n device inputs x -> y (device pointers, asynchronous on `stream`): bit-identical to the
  * host C library's expf (the one qwen.c calls) on every float. The first call per process builds the table of
- * the library's non-correctly-rounded results (all host threads, a few seconds; cached under $MVB_CACHE_DIR or
- * /tmp). entries/thresh (may be NULL) receive the table size and probe threshold. 0, or -1. */
+ * the library's non-correctly-rounded results (all host threads, a few seconds; cached in $MVB_CACHE_DIR, else
+ * $XDG_CACHE_HOME/mvb or ~/.cache/mvb, in a file only this user may write, checked before use). entries/thresh (may be NULL) receive the table size and probe threshold. 0, or -1. */
 int mvb_expf_eval(const float *x, float *y, int n, int *entries, float *thresh, void *stream);
 
 /* ---- Batched prefill matmul on the tensor cores ----

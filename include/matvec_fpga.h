@@ -12,7 +12,10 @@
  *     first used is not seen again.
  *   - xq and xs are uploaded on every call; out is copied back into the host buffer before the call returns.
  * Every call is synchronous and waits at most MATVEC_TIMEOUT_S seconds (default 5, like the reference's
- * TIMEOUT_S, driver/matvec_fpga.cpp:71). Not thread-safe, like the reference (one caller thread).
+ * TIMEOUT_S, driver/matvec_fpga.cpp:34). After a call that timed out, every later matvec call returns -1 until
+ * fpga_close(): that call's result copy may still be in flight. Not thread-safe, like the reference (one caller
+ * thread). MATVEC_STATS=1 makes fpga_close() print the mean per-call times (host enqueue, upload, kernel,
+ * download, completion wait) as one "matvec stats: {...}" line on stderr.
  */
 #ifndef MATVEC_FPGA_H
 #define MATVEC_FPGA_H
@@ -41,8 +44,9 @@ void *fpga_alloc_try(size_t bytes, uint64_t *phys);
 /* Replaces fpga_matvec (driver/matvec_fpga.h:26; contract hls/matvec.h:1-19, runq.c matmul):
  *   out[i] = sum over g of ((float)(sum_{k<gs} wq[i*n + g*gs + k] * xq[g*gs + k]) * ws[(i*n)/gs + g]) * xs[g]
  * int8 weights, fp32 weight scales, group size gs in {32, 64}; groups added in order, bit-exact with runq.c.
- * Rejects gs not 32/64, n <= 0, n > 8192, n % gs != 0, d <= 0, or an address outside every buffer.
- * Returns 0, or -1 with a message on stderr. */
+ * Rejects gs not 32/64, n <= 0, n > 8192, n % gs != 0, d <= 0 (the reference's checks), an address outside every
+ * buffer, or fp32 arrays ws/xs/out off their 4-byte alignment. wq and xq may sit at any byte address, as in the
+ * reference (a misaligned range is read from an aligned device copy). Returns 0, or -1 with a message on stderr. */
 int fpga_matvec(uint64_t wq, uint64_t ws, uint64_t xq, uint64_t xs, uint64_t out, int n, int d, int gs);
 
 /* Replaces fpga_matvec4 (driver/matvec_fpga.h:30; contract hls4/matvec4.h:1-21, qwen.c matmul_cpu):

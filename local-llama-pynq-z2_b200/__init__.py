@@ -99,6 +99,8 @@ def lib():
         L.mvb_qwen_trace.argtypes = [vp, i, i, C.POINTER(C.c_float)]
         L.mvb_qwen_profile.restype = i
         L.mvb_qwen_profile.argtypes = [vp, C.POINTER(C.c_float), i]
+        L.mvb_qwen_stamps.restype = i
+        L.mvb_qwen_stamps.argtypes = [vp, C.POINTER(C.c_double), i]
         L.mvb_qwen_kernel_info.restype = i
         L.mvb_qwen_kernel_info.argtypes = [vp, i, i, C.c_char_p, i, ip, C.POINTER(C.c_double)]
         L.mvb_gemm4.restype = i
@@ -434,6 +436,16 @@ class QwenDecoder:
         if n < 0:
             raise MatvecError("mvb_qwen_profile failed: " + last_error())
         return ms[:n]
+
+    def stamps(self):
+        """One step as the graph runs it, every kernel stamping the global timer: array (kernels, 2) of
+        (first CTA past its wait, last CTA done) in microseconds after the step's start."""
+        import numpy as np
+        us = np.zeros(2 * self.cfg["kernels_per_step"], np.float64)
+        n = lib().mvb_qwen_stamps(self.h, us.ctypes.data_as(C.POINTER(C.c_double)), us.size)
+        if n < 0:
+            raise MatvecError("mvb_qwen_stamps failed: " + last_error())
+        return us[:2 * n].reshape(n, 2)
 
     def trace(self, token, pos):
         """Residual stream after the embedding and after every attention / FFN block: [2 * n_layers + 1, dim]."""

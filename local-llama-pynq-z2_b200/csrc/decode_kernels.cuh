@@ -29,8 +29,6 @@ namespace decode {
 constexpr int kQwen = kXQuantizeQwen, kRunq = kXQuantizeRunq;
 
 constexpr int kImEnd = 151645, kEndOfText = 151643;  // qwen.c:31-32
-// rmsnorm'd vectors have at most 2048 elements: two passes of quantize_to_planes (kThreads / (GS / 4) groups each)
-constexpr int kNormPasses = 2;
 
 struct State {
     int token;       // token of the current position
@@ -42,85 +40,14 @@ struct State {
     int pad;
 };
 
-__device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
-
-// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of GS (32, or 64 for runq) like
-// qwen.c:355-364 (FAM kQwen) or runq.c:244-270 (kRunq) into a CTA's activation planes (matvec_kernels.cuh
-// layout: for int4 weights even/odd element planes, for int8 weights chunk planes) and the scales into xs; for
-// int4 weights also each group's sum of its int8 values into xsum (the nibble offset correction of the products).
-// GS/4 threads share a group, four consecutive elements each. The group maximum is taken over the float bits of
-// |v| (order-free and exact; NaN counts as 0, since qwen.c's fmaxf and runq.c's `>` ignore NaN), combined across
-// the group's threads with shuffles.
-// NORM: v is an rmsnorm's input and each element is first normalized as qwen.c:343 / runq.c:406 do,
-// fl(w * fl(sc * v)), with this thread's rmsnorm weights nw0 / nw1 (the four of its elements in the first /
-// second pass, see norm_weights_for_planes) and the inverse root sc; n is then at most kNormPasses passes of groups.
-// GSRC: v is the previous kernel's output in global memory, read with L2 loads (ld.global.cg: the lines may be
-// stale in this SM's L1), instead of a shared-memory copy.
-template <int BITS, int FAM, int GS, bool NORM, bool GSRC = false>
-__device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs, int *xsum,
-                                                   float4 nw0, float4 nw1, float sc) {
-    constexpr int TPG = GS / 4;  // threads per group
-    const int ng = n / GS, l = threadIdx.x % TPG;
-    for (int base = 0, pass = 0; base < ng; base += kThreads / TPG, pass++) {  // the same trip count in every
-                                                                               // thread (shuffles)
-        if (NORM && pass == kNormPasses) break;
-        const int g = base + threadIdx.x / TPG;
-        const bool on = g < ng;
-        float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (on) f = GSRC ? ld_cg4(v + GS * g + 4 * l) : reinterpret_cast<const float4 *>(v + GS * g)[l];
-        if (NORM) {
-            const float4 w = pass == 0 ? nw0 : nw1;  // a select of registers, not an indexed local array
-            f.x = __fmul_rn(w.x, __fmul_rn(sc, f.x));
-            f.y = __fmul_rn(w.y, __fmul_rn(sc, f.y));
-            f.z = __fmul_rn(w.z, __fmul_rn(sc, f.z));
-            f.w = __fmul_rn(w.w, __fmul_rn(sc, f.w));
-        }
-        auto bits = [](float x) {
-            const float a = fabsf(x);
-            return a == a ? __float_as_uint(a) : 0u;
-        };
-        unsigned m = max(max(bits(f.x), bits(f.y)), max(bits(f.z), bits(f.w)));
-        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        if (TPG == 16) m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
-        float scale;
-        uint32_t q0, q1, q2, q3;
-        if (FAM == kRunq) {  // runq.c: scale = wmax / 127, q = round(x / scale), no guard for a zero scale
-            scale = __fdiv_rn(__uint_as_float(m), 127.0f);
-            q0 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.x, scale)));
-            q1 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.y, scale)));
-            q2 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.z, scale)));
-            q3 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.w, scale)));
-        } else {
-            scale = __fmul_rn(__uint_as_float(m), 1.0f / 127.0f);
-            const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, same value
-            q0 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.x, inv)));
-            q1 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.y, inv)));
-            q2 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.z, inv)));
-            q3 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.w, inv)));
-        }
-        int sum = 0;
-        if (BITS == 4) {  // the group's sum of its int8 values: this thread's four, then across the group's threads
-            sum = (int)(int8_t)q0 + (int)(int8_t)q1 + (int)(int8_t)q2 + (int)(int8_t)q3;
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        }
-        if (on) {
-            if (BITS == 4) {
-                // elements 4l, 4l+2 are even-plane bytes 2l, 2l+1; elements 4l+1, 4l+3 odd-plane bytes 2l, 2l+1
-                *reinterpret_cast<uint16_t *>(planes + g * 16 + 2 * l) = (uint16_t)(q0 | q2 << 8);
-                *reinterpret_cast<uint16_t *>(planes + (ng + g) * 16 + 2 * l) = (uint16_t)(q1 | q3 << 8);
-                if (l == 0) xsum[g] = sum;
-            } else {
-                // elements 4l .. 4l+3 are bytes 4(l & 3) .. of chunk l >> 2
-                *reinterpret_cast<uint32_t *>(planes + ((l >> 2) * ng + g) * 16 + 4 * (l & 3)) =
-                    q0 | q1 << 8 | q2 << 16 | q3 << 24;
-            }
-            if (l == 0) xs[g] = scale;
-        }
-    }
+// Timing of the step as the graph runs it (only in the model's stamped copy of the step; null elsewhere): stamp[0]
+// keeps ~t of the earliest moment a CTA of the kernel got past its wait for the previous kernel, stamp[1] the
+// latest moment a CTA finished, both as atomic maxima of %globaltimer so that zeroed slots need no other setup.
+__device__ __forceinline__ void stamp_start(unsigned long long *stamp) {
+    if (stamp && threadIdx.x == 0) atomicMax(stamp, ~global_ns());
+}
+__device__ __forceinline__ void stamp_end(unsigned long long *stamp) {
+    if (stamp && threadIdx.x == 0) atomicMax(stamp + 1, global_ns());
 }
 
 // Quantizes a long v[0 .. n-1] (more groups of 32 than one pass of quantize_to_planes covers) into the same
@@ -216,20 +143,11 @@ __device__ __forceinline__ void norm_weights_for_planes(const float *norm_w, int
 template <int FAM, int GS>
 __device__ __forceinline__ void quantize_to_global(const float *v, int n, int8_t *xq, float *xs) {
     for (int g = threadIdx.x; g < n / GS; g += blockDim.x) {
-        int8_t q[GS];
-        xs[g] = quantize_group<GS>(v, g, FAM, q);
+        uint32_t q4[GS / 4];
+        xs[g] = quantize_group<GS>(v, g, FAM, q4);
         uint4 *dst = reinterpret_cast<uint4 *>(xq + GS * g);
 #pragma unroll
-        for (int c = 0; c < GS / 16; c++) {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int e = 16 * c + 4 * j;
-                w[j] = (uint32_t)(uint8_t)q[e] | (uint32_t)(uint8_t)q[e + 1] << 8 | (uint32_t)(uint8_t)q[e + 2] << 16 |
-                       (uint32_t)(uint8_t)q[e + 3] << 24;
-            }
-            dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+        for (int c = 0; c < GS / 16; c++) dst[c] = make_uint4(q4[4 * c], q4[4 * c + 1], q4[4 * c + 2], q4[4 * c + 3]);
     }
 }
 
@@ -273,9 +191,11 @@ __device__ __forceinline__ bool last_cta(int *counter) {
 // embedding row of the current token (qwen.c:498-501 with fp16 scales per 32, runq.c:490-492 with fp32 scales per
 // group of gs), exact in fp32; also clears the head's argmax key.
 template <int FAM>
-__global__ void embed_kernel(const int8_t *emb_q, const void *emb_s, float *x, int dim, int gs, State *st) {
+__global__ void embed_kernel(const int8_t *emb_q, const void *emb_s, float *x, int dim, int gs, State *st,
+                             unsigned long long *stamp) {
     allow_consumer();
     wait_for_producer();
+    stamp_start(stamp);
     const int tok = __ldcg(&st->token);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i == 0) st->key = 0ull;
@@ -285,6 +205,7 @@ __global__ void embed_kernel(const int8_t *emb_q, const void *emb_s, float *x, i
                                      : scale_from_f16(static_cast<const uint16_t *>(emb_s)[g]);
         x[i] = __fmul_rn(__int2float_rn(emb_q[r + i]), s);
     }
+    stamp_end(stamp);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -330,6 +251,7 @@ struct DecodeParams {
     const int32_t *head_ids;  // null: the argmax row is the token
     int *ids;
     int cap;
+    unsigned long long *stamp;  // this kernel's two timing slots (stamp_start / stamp_end), or null
 };
 
 // Bytes of a decode matvec CTA's per-group activation scales and int4 offset sums, padded to 16 so that the
@@ -394,6 +316,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     if (PRO == kProNorm) norm_weights_for_planes<GS>(p.norm_w, n, nw4);
     if (EPI == kEpiStore) allow_consumer();
     wait_for_producer();
+    stamp_start(p.stamp);
     // the residual's current value, loaded now so its latency overlaps the prologue
     float old = 0.0f;
     if (EPI == kEpiResidual && tid < rows) old = __ldcg(p.out + row0 + tid);
@@ -547,6 +470,9 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             const uint32_t b = __float_as_uint(c);
             const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
             if (c == c) key = ((unsigned long long)ord << 32) | (uint32_t)(~(uint32_t)(row0 + tid));
+            // The reference's scan starts from logit 0 and only moves on a strict `>`: a NaN there wins whatever
+            // follows (qwen.c:591-598, runq.c:843-854). The all-ones key beats every ordered value and names row 0.
+            else if (row0 + tid == 0) key = ~0ull;
         }
 #pragma unroll
         for (int off = 16; off; off >>= 1) {
@@ -557,7 +483,10 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     }
 
     // 5. the last CTA prepares the next kernel's input
-    if (TAIL == kTailNone || !last_cta(p.counter)) return;
+    if (TAIL == kTailNone || !last_cta(p.counter)) {
+        stamp_end(p.stamp);
+        return;
+    }
     float *sm = reinterpret_cast<float *>(smem);
     if (TAIL == kTailNormQuant) {
         for (int j = tid; j < p.d / 4; j += kThreads) reinterpret_cast<float4 *>(sm)[j] = ld_cg4(p.out + 4 * j);
@@ -566,7 +495,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         State *st = p.st;
         const int pos = st->pos;
         const unsigned long long key = atomicAdd(&st->key, 0ull);
-        // no key: every logit was NaN; the reference's strict `>` then keeps row 0 (qwen.c:591-598, runq.c:843-854)
+        // no key cannot happen (a NaN logit 0 gives the all-ones key); kept as row 0, the reference's answer
         const int row = key ? (int)(~(uint32_t)(key & 0xffffffffu)) : 0;
         st->last_row = row;
         if (st->n_prompt >= 0) {
@@ -582,6 +511,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
         }
         st->pos = pos + 1;
     }
+    stamp_end(p.stamp);
 }
 
 // Dynamic shared memory of decode_matvec_kernel for groups of gs: the product stage (plus x and the normalized x
@@ -612,6 +542,7 @@ struct AttnParams {
     int dim, kv_dim, kv_mul, ctx;
     State *st;
     ExpTable et;
+    unsigned long long *stamp;  // timing slots (stamp_start / stamp_end), or null
 };
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
@@ -718,6 +649,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
     }
     if (FAM == kQwen && tid < HS) bv0 = p.bv[kvh * HS + tid];
     wait_for_producer();
+    stamp_start(p.stamp);
     const float *qr = p.qkv + h * HS, *kr = p.qkv + p.dim + kvh * HS, *vr = p.qkv + p.dim + p.kv_dim + kvh * HS;
     // qwen.c adds the biases to the raw outputs (qwen.c:521-524); runq.c rotates them as they are (runq.c:506-521)
     auto in = [](const float *r, int i, float bias) {
@@ -804,6 +736,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnParams p)
         acc = __fadd_rn(acc, __fmul_rn(att[pos], vc[tid]));
         p.xb[h * HS + tid] = acc;
     }
+    stamp_end(p.stamp);
 }
 
 template <int HS>

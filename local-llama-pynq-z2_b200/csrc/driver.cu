@@ -1,9 +1,15 @@
 // The reference's board-driver C ABI (driver/matvec_fpga.h) served by a B200. See include/matvec_fpga.h for
 // the contract. Replaces driver/matvec_fpga.cpp:
-//   XRT/zocl CMA buffers (cpp:163-191)       -> pinned host buffer + HBM twin; "phys" = the twin's device address
-//   AXI-Lite register writes + ap_start (cpp:210-269) -> argument validation, host<->HBM copies, kernel launch
-//   ap_done busy poll with TIMEOUT_S (cpp:193-207)    -> cudaEventQuery poll against a deadline
-// State is process-global and not thread-safe, like the reference's static globals (cpp:87-93).
+//   XRT/zocl CMA buffers (fpga_alloc_try, cpp:126-148)          -> pinned host buffer + HBM twin; "phys" = the
+//                                                                 twin's device address
+//   AXI-Lite register writes + ap_start (fpga_matvec, cpp:173-199; fpga_matvec4, cpp:207-233)
+//                                                               -> argument validation, host<->HBM copies, launch
+//   ap_done busy poll with TIMEOUT_S (run_kernel, cpp:157-171)  -> cudaEventQuery poll against a deadline
+// State is process-global and not thread-safe, like the reference's static globals (cpp:50-56).
+//
+// MATVEC_STATS=1 (environment, read by fpga_open) times every call: host time to enqueue, device time of the
+// activation upload, the kernel and the result download (CUDA events), and the wait for completion; fpga_close()
+// prints the means over the calls that uploaded no weights as one "matvec stats: {...}" JSON line on stderr.
 #include <errno.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -27,17 +33,30 @@ struct Buffer {
     size_t size;
 };
 
+struct Stats {
+    cudaEvent_t ev[4] = {};  // before the activation upload, before the launch, after the kernel, after the download
+    double calls = 0, enqueue_us = 0, h2d_us = 0, kernel_us = 0, d2h_us = 0, wait_us = 0, total_us = 0;
+    double upload_calls = 0;  // calls that also uploaded weights (first use), left out of the means
+};
+
 struct Driver {
     bool open = false;
+    bool failed = false;                     // a call timed out: its copies may still land, so refuse further calls
     int device = 0;
     cudaStream_t stream = nullptr;
     cudaEvent_t done = nullptr;
     std::map<uint64_t, Buffer> bufs;         // keyed by device base address
     std::map<uint64_t, uint64_t> resident;   // weight byte ranges [first, second) already uploaded (merged)
+    // weight ranges whose device address is not 16-byte aligned (fpga_matvec accepts any int8 address, as the
+    // reference does): an aligned device copy per range, made on first use, keyed by (address, length)
+    std::map<std::pair<uint64_t, size_t>, void *> shadows;
+    int8_t *xstage = nullptr;                // aligned device staging for misaligned activations (MAX_N + scales)
     size_t total = 0;
     size_t limit = 0;                        // MATVEC_ALLOC_LIMIT, 0 = none
-    double timeout_s = 5.0;                  // MATVEC_TIMEOUT_S, reference TIMEOUT_S (cpp:71)
+    double timeout_s = 5.0;                  // MATVEC_TIMEOUT_S, reference TIMEOUT_S (cpp:34)
     char last_alloc_err[256] = "";
+    bool stats_on = false;                   // MATVEC_STATS
+    Stats stats;
 };
 
 Driver drv;
@@ -59,13 +78,15 @@ Buffer *resolve(uint64_t addr, size_t len) {
 }
 
 // Uploads [addr, addr + len) unless a previous call already did; weights are immutable after first use.
-bool ensure_resident(const Buffer &b, uint64_t addr, size_t len) {
+// *uploaded is set when this call copied anything.
+bool ensure_resident(const Buffer &b, uint64_t addr, size_t len, bool *uploaded) {
     const uint64_t end = addr + len;
     auto it = drv.resident.upper_bound(addr);
     if (it != drv.resident.begin()) {
         auto prev = std::prev(it);
         if (prev->first <= addr && prev->second >= end) return true;
     }
+    *uploaded = true;
     cudaError_t e = cudaMemcpyAsync((void *)addr, b.host + (addr - b.dev), len, cudaMemcpyHostToDevice, drv.stream);
     if (e != cudaSuccess) return false;
     // insert [addr, end) and merge with overlapping or touching neighbours
@@ -105,14 +126,37 @@ int wait_done(const char *who, int n, int d, int arg, const char *argname) {
         }
         if (i % 256 == 0 && now_s() > deadline) {
             set_error("%s: kernel did not finish in %g s (n=%d d=%d %s=%d)", who, drv.timeout_s, n, d, argname, arg);
+            drv.failed = true;  // its result download is still queued: no later call may reuse the buffers
             return -1;
         }
     }
 }
 
+// An aligned device copy of the weight range [addr, addr + len) of buffer b (whose device address is misaligned),
+// made on first use; null on failure.
+void *shadow_of(const Buffer &b, uint64_t addr, size_t len, bool *uploaded) {
+    const auto key = std::make_pair(addr, len);
+    auto it = drv.shadows.find(key);
+    if (it != drv.shadows.end()) return it->second;
+    void *p = nullptr;
+    if (cudaMalloc(&p, len) != cudaSuccess) return nullptr;
+    if (cudaMemcpyAsync(p, b.host + (addr - b.dev), len, cudaMemcpyHostToDevice, drv.stream) != cudaSuccess) {
+        cudaFree(p);
+        return nullptr;
+    }
+    *uploaded = true;
+    drv.shadows[key] = p;
+    return p;
+}
+
 // One synchronous matvec through host buffers: weights resident, activations up, result down.
 int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t xq, uint64_t xs, uint64_t out,
              int n, int d, int arg, const char *argname) {
+    if (drv.failed) {
+        set_error("%s: an earlier call timed out and its copies may still be in flight; call fpga_close()", who);
+        return -1;
+    }
+    const double t_entry = drv.stats_on ? now_s() : 0.0;
     const int ng = n / gs;
     const size_t wbytes = (size_t)d * n * (fmt == kQ4F16 ? 4 : 8) / 8;
     const size_t sbytes = (size_t)d * ng * (fmt == kQ8F32 ? 4 : 2);
@@ -123,12 +167,31 @@ int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t
                   bw ? "" : "w ", bs ? "" : "ws ", bq ? "" : "xq ", bx ? "" : "xs ", bo ? "" : "out");
         return -1;
     }
-    if (!ensure_resident(*bw, w, wbytes) || !ensure_resident(*bs, ws, sbytes)) {
+    bool uploaded = false;
+    const void *wdev = (const void *)w;
+    if (w & 15) {  // a misaligned int8 plane (fpga_matvec only; fpga_matvec4 requires 64-byte alignment)
+        wdev = shadow_of(*bw, w, wbytes, &uploaded);
+        if (!wdev) {
+            set_error("%s: cannot make an aligned copy of the weights at a misaligned address", who);
+            return -1;
+        }
+    } else if (!ensure_resident(*bw, w, wbytes, &uploaded)) {
+        set_error("%s: weight upload failed: %s", who, cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    if (!ensure_resident(*bs, ws, sbytes, &uploaded)) {
         set_error("%s: weight upload failed: %s", who, cudaGetErrorString(cudaGetLastError()));
         return -1;
     }
     cudaError_t e;
-    if (bq == bx && xs >= xq && xs - xq <= 65536) {  // one copy when the scales sit just after the values
+    if (drv.stats_on) cudaEventRecord(drv.stats.ev[0], drv.stream);
+    const void *xqdev = (const void *)xq;
+    if (xq & 15) {  // a misaligned int8 activation vector: staged at an aligned device address instead
+        e = cudaMemcpyAsync(drv.xstage, bq->host + (xq - bq->dev), n, cudaMemcpyHostToDevice, drv.stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync((void *)xs, bx->host + (xs - bx->dev), ng * 4, cudaMemcpyHostToDevice, drv.stream);
+        xqdev = drv.xstage;
+    } else if (bq == bx && xs >= xq && xs - xq <= 65536) {  // one copy when the scales sit just after the values
         e = cudaMemcpyAsync((void *)xq, bq->host + (xq - bq->dev), xs + ng * 4 - xq, cudaMemcpyHostToDevice,
                             drv.stream);
     } else {
@@ -140,16 +203,38 @@ int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t
         set_error("%s: activation upload failed: %s", who, cudaGetErrorString(e));
         return -1;
     }
-    if (launch_matvec(who, fmt, gs, (const void *)w, (const void *)ws, (const void *)xq, (const void *)xs, nullptr,
-                      (float *)out, n, d, kXQuantized, drv.stream) != 0)
+    if (drv.stats_on) cudaEventRecord(drv.stats.ev[1], drv.stream);
+    if (launch_matvec(who, fmt, gs, wdev, (const void *)ws, xqdev, (const void *)xs, nullptr, (float *)out, n, d,
+                      kXQuantized, drv.stream) != 0)
         return -1;
+    if (drv.stats_on) cudaEventRecord(drv.stats.ev[2], drv.stream);
     e = cudaMemcpyAsync(bo->host + (out - bo->dev), (const void *)out, (size_t)d * 4, cudaMemcpyDeviceToHost,
                         drv.stream);
     if (e != cudaSuccess) {
         set_error("%s: result download failed: %s", who, cudaGetErrorString(e));
         return -1;
     }
-    return wait_done(who, n, d, arg, argname);
+    if (drv.stats_on) cudaEventRecord(drv.stats.ev[3], drv.stream);
+    const double t_enq = drv.stats_on ? now_s() : 0.0;
+    const int rc = wait_done(who, n, d, arg, argname);
+    if (rc == 0 && drv.stats_on) {
+        Stats &st = drv.stats;
+        if (uploaded) {
+            st.upload_calls++;
+        } else {
+            const double t_done = now_s();
+            float ms[3] = {0, 0, 0};
+            for (int i = 0; i < 3; i++) cudaEventElapsedTime(&ms[i], st.ev[i], st.ev[i + 1]);
+            st.calls++;
+            st.enqueue_us += (t_enq - t_entry) * 1e6;
+            st.wait_us += (t_done - t_enq) * 1e6;
+            st.total_us += (t_done - t_entry) * 1e6;
+            st.h2d_us += ms[0] * 1e3;
+            st.kernel_us += ms[1] * 1e3;
+            st.d2h_us += ms[2] * 1e3;
+        }
+    }
+    return rc;
 }
 
 bool env_number(const char *name, double *out) {
@@ -168,7 +253,7 @@ bool env_number(const char *name, double *out) {
 extern "C" int fpga_open(void) {
     if (drv.open) return 0;
     int dev = 0;
-    if (const char *e = getenv("FPGA_MEMIDX")) {  // reference: memory bank index (cpp:120-128)
+    if (const char *e = getenv("FPGA_MEMIDX")) {  // reference: memory bank index (cpp:83-91)
         char *end;
         long v = strtol(e, &end, 0);
         if (!*e || *end || v < 0) {
@@ -183,18 +268,28 @@ extern "C" int fpga_open(void) {
         set_error("fpga: no CUDA device %d (%s)", dev, err != cudaSuccess ? cudaGetErrorString(err) : "out of range");
         return -1;
     }
-    double limit = 0, timeout = 5.0;
-    if (!env_number("MATVEC_ALLOC_LIMIT", &limit) || !env_number("MATVEC_TIMEOUT_S", &timeout) || timeout <= 0) {
-        set_error("fpga: bad MATVEC_ALLOC_LIMIT or MATVEC_TIMEOUT_S");
+    double limit = 0, timeout = 5.0, stats = 0;
+    if (!env_number("MATVEC_ALLOC_LIMIT", &limit) || !env_number("MATVEC_TIMEOUT_S", &timeout) || timeout <= 0 ||
+        !env_number("MATVEC_STATS", &stats)) {
+        set_error("fpga: bad MATVEC_ALLOC_LIMIT, MATVEC_TIMEOUT_S or MATVEC_STATS");
         return -1;
     }
     if ((err = cudaSetDevice(dev)) != cudaSuccess ||
         (err = cudaStreamCreateWithFlags(&drv.stream, cudaStreamNonBlocking)) != cudaSuccess ||
-        (err = cudaEventCreateWithFlags(&drv.done, cudaEventDisableTiming)) != cudaSuccess) {
+        (err = cudaEventCreateWithFlags(&drv.done, cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaMalloc(&drv.xstage, kMaxN + kMaxN / 32 * 4)) != cudaSuccess) {
         set_error("fpga: cannot open CUDA device %d: %s", dev, cudaGetErrorString(err));
         fpga_close();
         return -1;
     }
+    drv.stats_on = stats != 0;
+    drv.stats = Stats{};
+    for (int i = 0; drv.stats_on && i < 4; i++)
+        if ((err = cudaEventCreate(&drv.stats.ev[i])) != cudaSuccess) {
+            set_error("fpga: cannot create timing events: %s", cudaGetErrorString(err));
+            fpga_close();
+            return -1;
+        }
     drv.device = dev;
     drv.limit = (size_t)limit;
     drv.timeout_s = timeout;
@@ -246,13 +341,16 @@ extern "C" int fpga_matvec(uint64_t wq, uint64_t ws, uint64_t xq, uint64_t xs, u
         set_error("fpga_matvec: fpga_open() not called");
         return -1;
     }
-    if ((gs != 32 && gs != 64) || n <= 0 || n > kMaxN || n % gs || d <= 0) {  // reference checks (cpp:215-219)
+    if ((gs != 32 && gs != 64) || n <= 0 || n > kMaxN || n % gs || d <= 0) {  // reference checks (cpp:178-182)
         set_error("fpga_matvec: unsupported n=%d d=%d gs=%d (need gs 32 or 64, n %% gs == 0, n <= %d)", n, d, gs,
                   kMaxN);
         return -1;
     }
-    if ((wq | xq) & 15 || (ws | xs | out) & 3) {  // the reference's AXI bursts need no alignment; 128-bit loads do
-        set_error("fpga_matvec: wq/xq must be 16-byte and ws/xs/out 4-byte aligned");
+    // The reference checks no alignment (cpp:178); neither is wq/xq's needed here (a misaligned int8 plane or
+    // vector is read from an aligned device copy). The fp32 arrays ws/xs/out must sit on 4 bytes, as the host's own
+    // float pointers at the same offsets must for C.
+    if ((ws | xs | out) & 3) {
+        set_error("fpga_matvec: ws/xs/out must be 4-byte aligned (fp32 arrays)");
         return -1;
     }
     return run_call("fpga_matvec", kQ8F32, gs, wq, ws, xq, xs, out, n, d, gs, "gs");
@@ -264,6 +362,7 @@ extern "C" int fpga_matvec4(uint64_t w, uint64_t ws, uint64_t xq, uint64_t xs, u
         set_error("fpga_matvec4: fpga_open() not called");
         return -1;
     }
+    // the reference's checks (cpp:212-216)
     if ((wbits != 4 && wbits != 8) || n <= 0 || n > kMaxN || n % 32 || d <= 0 || ((w | ws | xq | xs | out) & 63)) {
         set_error("fpga_matvec4: unsupported n=%d d=%d wbits=%d or a buffer not 64-byte aligned "
                   "(need wbits 4 or 8, n %% 32 == 0, n <= %d)", n, d, wbits, kMaxN);
@@ -274,10 +373,28 @@ extern "C" int fpga_matvec4(uint64_t w, uint64_t ws, uint64_t xq, uint64_t xs, u
 
 extern "C" void fpga_close(void) {
     if (drv.stream) cudaStreamSynchronize(drv.stream);
+    if (drv.stats_on) {
+        const Stats &st = drv.stats;
+        const double c = st.calls > 0 ? st.calls : 1;
+        fprintf(stderr,
+                "matvec stats: {\"calls\": %.0f, \"us_per_call\": %.2f, \"host_enqueue_us\": %.2f, \"h2d_us\": %.2f, "
+                "\"kernel_us\": %.2f, \"d2h_us\": %.2f, \"completion_wait_us\": %.2f, \"calls_with_weight_upload\": "
+                "%.0f}\n",
+                st.calls, st.total_us / c, st.enqueue_us / c, st.h2d_us / c, st.kernel_us / c, st.d2h_us / c,
+                st.wait_us / c, st.upload_calls);
+        for (cudaEvent_t e : st.ev)
+            if (e) cudaEventDestroy(e);
+        drv.stats = Stats{};
+        drv.stats_on = false;
+    }
     for (auto &kv : drv.bufs) {
         cudaFreeHost(kv.second.host);
         cudaFree((void *)kv.second.dev);
     }
+    for (auto &kv : drv.shadows) cudaFree(kv.second);
+    drv.shadows.clear();
+    if (drv.xstage) cudaFree(drv.xstage);
+    drv.xstage = nullptr;
     drv.bufs.clear();
     drv.resident.clear();
     if (drv.done) cudaEventDestroy(drv.done);
@@ -285,5 +402,6 @@ extern "C" void fpga_close(void) {
     drv.done = nullptr;
     drv.stream = nullptr;
     drv.total = 0;
+    drv.failed = false;
     drv.open = false;
 }

@@ -1,10 +1,17 @@
 // Host side of expf_ref.h: the table of inputs where the host C library's expf is not the correctly rounded
 // value (or where the exact value sits within 2^-40 of a rounding midpoint), built by calling that expf on every
 // float of [-104, 89] with all host threads, cached on disk, and uploaded as an open-addressing hash table.
+//
+// The cache lives in $MVB_CACHE_DIR, else $XDG_CACHE_HOME/mvb, else $HOME/.cache/mvb (made 0700), as a file made
+// 0600; a cache file is used only if this user owns it, nobody else may write it, its length matches its entry
+// count, every key lies in the table's domain and its checksum matches. Anything else is rebuilt.
+#include <errno.h>
+#include <fcntl.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/stat.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -21,7 +28,7 @@ namespace mvb {
 namespace {
 
 constexpr float kLo = -104.0f, kHi = 89.0f;
-constexpr uint32_t kMagic = 0x31465845u;  // "EXF1"
+constexpr uint32_t kMagic = 0x32465845u;  // "EXF2": header, entries, then a checksum
 
 struct Entry {
     uint32_t key, val;
@@ -35,7 +42,7 @@ struct HostTable {
 
 std::mutex g_mu;
 HostTable g_host;
-std::map<int, ExpTable> g_dev;
+std::map<unsigned long long, ExpTable> g_dev;  // the uploaded table of each CUDA context (by unique context ID)
 
 uint32_t bits(float f) {
     uint32_t u;
@@ -88,33 +95,91 @@ std::string fingerprint() {
     return s;
 }
 
+// The cache directory (created 0700 where it is this library's own), or "" if there is none.
+std::string cache_dir() {
+    const char *d = getenv("MVB_CACHE_DIR");
+    if (d && *d) return d;
+    std::string base;
+    if ((d = getenv("XDG_CACHE_HOME")) && *d) base = d;
+    else if ((d = getenv("HOME")) && *d) base = std::string(d) + "/.cache";
+    else return "";
+    mkdir(base.c_str(), 0700);  // may exist already
+    const std::string dir = base + "/mvb";
+    if (mkdir(dir.c_str(), 0700) != 0 && errno != EEXIST) return "";
+    return dir;
+}
+
 std::string cache_path() {
-    const char *dir = getenv("MVB_CACHE_DIR");
-    return std::string(dir && *dir ? dir : "/tmp") + "/mvb_expf_v1_" + fingerprint() + ".bin";
+    const std::string dir = cache_dir();
+    return dir.empty() ? "" : dir + "/expf_v2_" + fingerprint() + ".bin";
+}
+
+uint64_t checksum(const HostTable &t) {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](uint32_t v) { h = (h ^ v) * 1099511628211ull; };
+    mix(bits(t.max_delta));
+    for (const Entry &e : t.entries) {
+        mix(e.key);
+        mix(e.val);
+    }
+    return h;
+}
+
+// A key of the table's domain: the bits of a float in [-104, -0] or [+0, 89].
+bool in_domain(uint32_t key) {
+    return (key >= bits(-0.0f) && key <= bits(kLo)) || key <= bits(kHi);
 }
 
 bool load_cache(HostTable *t) {
-    FILE *f = fopen(cache_path().c_str(), "rb");
-    if (!f) return false;
+    const std::string path = cache_path();
+    if (path.empty()) return false;
+    const int fd = open(path.c_str(), O_RDONLY | O_NOFOLLOW);
+    if (fd < 0) return false;
+    struct stat st;
+    FILE *f = fstat(fd, &st) == 0 ? fdopen(fd, "rb") : nullptr;
+    if (!f) {
+        close(fd);
+        return false;
+    }
     uint32_t hdr[2];
     float md;
-    bool ok = fread(hdr, 4, 2, f) == 2 && hdr[0] == kMagic && fread(&md, 4, 1, f) == 1;
+    uint64_t sum = 0;
+    // owned by this user, writable by nobody else, a regular file whose length matches its entry count
+    bool ok = S_ISREG(st.st_mode) && st.st_uid == geteuid() && !(st.st_mode & 022) && fread(hdr, 4, 2, f) == 2 &&
+              hdr[0] == kMagic && fread(&md, 4, 1, f) == 1 && md >= 0.0f && md <= 1.0f &&
+              (uint64_t)st.st_size == 12 + (uint64_t)hdr[1] * sizeof(Entry) + 8 && hdr[1] < (1u << 24);
     if (ok) {
         t->entries.resize(hdr[1]);
-        ok = fread(t->entries.data(), sizeof(Entry), hdr[1], f) == hdr[1];
         t->max_delta = md;
+        ok = fread(t->entries.data(), sizeof(Entry), hdr[1], f) == hdr[1] && fread(&sum, 8, 1, f) == 1 &&
+             sum == checksum(*t);
+        for (size_t i = 0; ok && i < t->entries.size(); i++) ok = in_domain(t->entries[i].key);
     }
     fclose(f);
+    if (!ok) {
+        t->entries.clear();
+        t->max_delta = 0.0f;
+    }
     return ok;
 }
 
 void save_cache(const HostTable &t) {
-    const std::string path = cache_path(), tmp = path + ".tmp" + std::to_string((long)getpid());
-    FILE *f = fopen(tmp.c_str(), "wb");
-    if (!f) return;
+    const std::string path = cache_path();
+    if (path.empty()) return;
+    const std::string tmp = path + ".tmp" + std::to_string((long)getpid());
+    const int fd = open(tmp.c_str(), O_WRONLY | O_CREAT | O_EXCL | O_NOFOLLOW, 0600);
+    if (fd < 0) return;
+    FILE *f = fdopen(fd, "wb");
+    if (!f) {
+        close(fd);
+        remove(tmp.c_str());
+        return;
+    }
     const uint32_t hdr[2] = {kMagic, (uint32_t)t.entries.size()};
+    const uint64_t sum = checksum(t);
     bool ok = fwrite(hdr, 4, 2, f) == 2 && fwrite(&t.max_delta, 4, 1, f) == 1 &&
-              fwrite(t.entries.data(), sizeof(Entry), t.entries.size(), f) == t.entries.size();
+              fwrite(t.entries.data(), sizeof(Entry), t.entries.size(), f) == t.entries.size() &&
+              fwrite(&sum, 8, 1, f) == 1;
     ok = fclose(f) == 0 && ok;
     if (ok) rename(tmp.c_str(), path.c_str());
     else remove(tmp.c_str());
@@ -157,7 +222,9 @@ ExpTable expf_table_device() {
     ExpTable t = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return t;
-    auto it = g_dev.find(dev);
+    // a table uploaded in an earlier context of this device (before a cudaDeviceReset) is gone: key by context
+    const unsigned long long ctx = current_context_id();
+    auto it = ctx ? g_dev.find(ctx) : g_dev.end();
     if (it != g_dev.end()) return it->second;
     build_host();
     uint32_t slots = 1;
@@ -190,7 +257,8 @@ ExpTable expf_table_device() {
     t.thresh = g_host.max_delta < 0.25f ? g_host.max_delta + 1e-4f : 1.0f;
     t.lo = kLo;
     t.hi = kHi;
-    g_dev[dev] = t;
+    const unsigned long long ctx_now = current_context_id();  // the upload made the context current if needed
+    if (ctx_now) g_dev[ctx_now] = t;
     return t;
 }
 

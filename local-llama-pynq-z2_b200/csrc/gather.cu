@@ -66,12 +66,6 @@ __device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned *p) {
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) gather_matvec_kernel(const GatherParams gp) {
     extern __shared__ __align__(16) uint8_t smem[];

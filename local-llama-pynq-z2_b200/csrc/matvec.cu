@@ -7,6 +7,9 @@
 #include <mutex>
 #include <tuple>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "../../include/matvec_b200.h"
 #include "matvec_kernels.cuh"
 #include "mvb_runtime.h"
@@ -26,6 +29,27 @@ void set_error(const char *fmt, ...) {
 void clear_error() { g_err[0] = 0; }
 
 const char *last_error() { return g_err; }
+
+unsigned long long current_context_id() {
+    static std::once_flag once;
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(f);
+    });
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 
 // Resident CTAs of `kernel` on the current device at kThreads threads and `smem` bytes (all SMs), cached per
 // device, kernel and size; 148 * 4 if the device cannot be queried.

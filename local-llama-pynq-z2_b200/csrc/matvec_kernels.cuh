@@ -5,7 +5,7 @@
 //     isum_g = sum_{k<gs} w[i, g*gs + k] * xq[g*gs + k]           int32, exact
 //     p_g    = ((float)isum_g * wscale[i, g]) * xs[g]             two fp32 multiplies, each rounded (no FMA)
 //     out[i] = (((0 + p_0) + p_1) + ...) + p_{ng-1}               fp32 adds in group order
-// The HLS kernels (hls4/matvec4.cpp:128-151, hls/matvec.cpp:320-344) compute the same sum; the int4 one adds
+// The HLS kernels (hls4/matvec4.cpp:107-131, hls/matvec.cpp:82-106) compute the same sum; the int4 one adds
 // in a tree order, which the reference checks with a tolerance. Here the order is always the sequential one.
 //
 // Work decomposition: a CTA owns a tile of `rt` consecutive rows. Because rows are contiguous in the weight
@@ -35,7 +35,7 @@ enum XMode : int {
 };
 
 constexpr int kThreads = 256;
-constexpr int kMaxN = 8192;  // MAX_N of driver/matvec_fpga.cpp:70
+constexpr int kMaxN = 8192;  // MAX_N of driver/matvec_fpga.cpp:33
 
 struct MatvecParams {
     const uint8_t *w;   // weight plane, row-major, d rows of n*bits/8 bytes
@@ -82,6 +82,13 @@ __device__ __forceinline__ float ld_f32(const void *p) {
 // Programmatic dependent launch: a no-op unless the launch carries the programmatic-serialization attribute.
 __device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_consumer() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Nanoseconds of the GPU's global timer (the same clock on every SM).
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 // Shared-memory loads by shared-window address. Volatile, so that they stay after the barriers that publish
 // the data (the compiler sees no memory access in an asm statement).
@@ -178,31 +185,114 @@ __device__ __forceinline__ int8_t to_int8_x86(float r) {
 }
 
 // Quantizes group g of x into 32 (or 64) int8 values and one scale, as qwen.c:355-364 (kXQuantizeQwen) or
-// runq.c:244-270 (kXQuantizeRunq) do; writes the values to q (registers) and returns the scale.
+// runq.c:244-270 (kXQuantizeRunq) do; writes the values packed four to a word to q4 (word j holds elements 4j ..
+// 4j + 3, element 4j + k in byte k) and returns the scale. The group is read twice (its maximum, then the values)
+// rather than held in registers, so a group of 64 costs no more registers than one of 32.
 template <int GS>
-__device__ __forceinline__ float quantize_group(const float *x, int g, int mode, int8_t (&q)[GS]) {
-    float v[GS];
+__device__ __forceinline__ float quantize_group(const float *x, int g, int mode, uint32_t (&q4)[GS / 4]) {
     const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)g * GS);
+    float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < GS / 4; i++) {
         const float4 f = src[i];
-        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        amax = fmaxf(fmaxf(amax, fabsf(f.x)), fmaxf(fabsf(f.y), fmaxf(fabsf(f.z), fabsf(f.w))));
     }
-    float amax = 0.0f;
+    const bool qwen = mode == kXQuantizeQwen;
+    const float scale = qwen ? __fmul_rn(amax, 1.0f / 127.0f) : __fdiv_rn(amax, 127.0f);
+    const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, correctly rounded either way
+    auto q = [&](float v) -> uint32_t {
+        return (uint8_t)to_int8_x86(roundf(qwen ? __fmul_rn(v, inv) : __fdiv_rn(v, scale)));
+    };
 #pragma unroll
-    for (int i = 0; i < GS; i++) amax = fmaxf(amax, fabsf(v[i]));
-    float scale;
-    if (mode == kXQuantizeQwen) {
-        scale = __fmul_rn(amax, 1.0f / 127.0f);
-        const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // 1.0f / scale, correctly rounded either way
-#pragma unroll
-        for (int i = 0; i < GS; i++) q[i] = to_int8_x86(roundf(__fmul_rn(v[i], inv)));
-    } else {
-        scale = __fdiv_rn(amax, 127.0f);
-#pragma unroll
-        for (int i = 0; i < GS; i++) q[i] = to_int8_x86(roundf(__fdiv_rn(v[i], scale)));
+    for (int i = 0; i < GS / 4; i++) {
+        const float4 f = src[i];
+        q4[i] = q(f.x) | q(f.y) << 8 | q(f.z) << 16 | q(f.w) << 24;
     }
     return scale;
+}
+
+__device__ __forceinline__ float4 ld_cg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+
+// rmsnorm'd vectors have at most 2048 elements: two passes of quantize_to_planes (kThreads / (GS / 4) groups each)
+constexpr int kNormPasses = 2;
+
+// Quantizes v[0 .. n-1] (shared memory, 16-byte aligned) per group of GS (32, or 64 for runq) like
+// qwen.c:355-364 (FAM kXQuantizeQwen) or runq.c:244-270 (kXQuantizeRunq) into a CTA's activation planes (the
+// layout above: for int4 weights even/odd element planes, for int8 weights chunk planes) and the scales into xs; for
+// int4 weights also each group's sum of its int8 values into xsum (the nibble offset correction of the products).
+// GS/4 threads share a group, four consecutive elements each. The group maximum is taken over the float bits of
+// |v| (order-free and exact; NaN counts as 0, since qwen.c's fmaxf and runq.c's `>` ignore NaN), combined across
+// the group's threads with shuffles.
+// NORM: v is an rmsnorm's input and each element is first normalized as qwen.c:343 / runq.c:406 do,
+// fl(w * fl(sc * v)), with this thread's rmsnorm weights nw0 / nw1 (the four of its elements in the first /
+// second pass, see norm_weights_for_planes) and the inverse root sc; n is then at most kNormPasses passes of groups.
+// GSRC: v is the previous kernel's output in global memory, read with L2 loads (ld.global.cg: the lines may be
+// stale in this SM's L1), instead of a shared-memory copy.
+template <int BITS, int FAM, int GS, bool NORM, bool GSRC = false>
+__device__ __forceinline__ void quantize_to_planes(const float *v, int n, uint8_t *planes, float *xs, int *xsum,
+                                                   float4 nw0, float4 nw1, float sc) {
+    constexpr int TPG = GS / 4;  // threads per group
+    const int ng = n / GS, l = threadIdx.x % TPG;
+    for (int base = 0, pass = 0; base < ng; base += kThreads / TPG, pass++) {  // the same trip count in every
+                                                                               // thread (shuffles)
+        if (NORM && pass == kNormPasses) break;
+        const int g = base + threadIdx.x / TPG;
+        const bool on = g < ng;
+        float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (on) f = GSRC ? ld_cg4(v + GS * g + 4 * l) : reinterpret_cast<const float4 *>(v + GS * g)[l];
+        if (NORM) {
+            const float4 w = pass == 0 ? nw0 : nw1;  // a select of registers, not an indexed local array
+            f.x = __fmul_rn(w.x, __fmul_rn(sc, f.x));
+            f.y = __fmul_rn(w.y, __fmul_rn(sc, f.y));
+            f.z = __fmul_rn(w.z, __fmul_rn(sc, f.z));
+            f.w = __fmul_rn(w.w, __fmul_rn(sc, f.w));
+        }
+        auto bits = [](float x) {
+            const float a = fabsf(x);
+            return a == a ? __float_as_uint(a) : 0u;
+        };
+        unsigned m = max(max(bits(f.x), bits(f.y)), max(bits(f.z), bits(f.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        if (TPG == 16) m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        float scale;
+        uint32_t q0, q1, q2, q3;
+        if (FAM == kXQuantizeRunq) {  // runq.c: scale = wmax / 127, q = round(x / scale), no guard for a zero scale
+            scale = __fdiv_rn(__uint_as_float(m), 127.0f);
+            q0 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.x, scale)));
+            q1 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.y, scale)));
+            q2 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.z, scale)));
+            q3 = (uint8_t)to_int8_x86(roundf(__fdiv_rn(f.w, scale)));
+        } else {
+            scale = __fmul_rn(__uint_as_float(m), 1.0f / 127.0f);
+            const float inv = scale > 0.0f ? __frcp_rn(scale) : 0.0f;  // qwen.c's 1.0f / scale, same value
+            q0 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.x, inv)));
+            q1 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.y, inv)));
+            q2 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.z, inv)));
+            q3 = (uint8_t)to_int8_x86(roundf(__fmul_rn(f.w, inv)));
+        }
+        int sum = 0;
+        if (BITS == 4) {  // the group's sum of its int8 values: this thread's four, then across the group's threads
+            sum = (int)(int8_t)q0 + (int)(int8_t)q1 + (int)(int8_t)q2 + (int)(int8_t)q3;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        }
+        if (on) {
+            if (BITS == 4) {
+                // elements 4l, 4l+2 are even-plane bytes 2l, 2l+1; elements 4l+1, 4l+3 odd-plane bytes 2l, 2l+1
+                *reinterpret_cast<uint16_t *>(planes + g * 16 + 2 * l) = (uint16_t)(q0 | q2 << 8);
+                *reinterpret_cast<uint16_t *>(planes + (ng + g) * 16 + 2 * l) = (uint16_t)(q1 | q3 << 8);
+                if (l == 0) xsum[g] = sum;
+            } else {
+                // elements 4l .. 4l+3 are bytes 4(l & 3) .. of chunk l >> 2
+                *reinterpret_cast<uint32_t *>(planes + ((l >> 2) * ng + g) * 16 + 4 * (l & 3)) =
+                    q0 | q1 << 8 | q2 << 16 | q3 << 24;
+            }
+            if (l == 0) xs[g] = scale;
+        }
+    }
 }
 
 // Resident CTAs per SM the compiler must allow (registers <= 64K / (256 * n)), per format: measured best on B200
@@ -256,32 +346,13 @@ __device__ __forceinline__ void stage_activations(const MatvecParams &p, const M
         }
         for (int g = tid; g < ng; g += kThreads) sm.xs[g] = p.xs[g];
     } else {
-        for (int g = tid; g < ng; g += kThreads) {
-            int8_t q[GS];
-            sm.xs[g] = quantize_group<GS>(p.x, g, XM, q);
-            uint32_t wv[GS / 4];
-#pragma unroll
-            for (int j = 0; j < GS / 4; j++)
-                wv[j] = (uint32_t)(uint8_t)q[4 * j] | (uint32_t)(uint8_t)q[4 * j + 1] << 8 |
-                        (uint32_t)(uint8_t)q[4 * j + 2] << 16 | (uint32_t)(uint8_t)q[4 * j + 3] << 24;
-#pragma unroll
-            for (int k = 0; k < XC; k++) {
-                uint4 a = make_uint4(wv[4 * k], wv[4 * k + 1], wv[4 * k + 2], wv[4 * k + 3]);
-                if (FMT == kQ4F16) {
-                    uint32_t *ev = reinterpret_cast<uint32_t *>(&xplane[g]) + 2 * k;
-                    uint32_t *od = reinterpret_cast<uint32_t *>(&xplane[ng + g]) + 2 * k;
-                    ev[0] = __byte_perm(a.x, a.y, 0x6420);
-                    ev[1] = __byte_perm(a.z, a.w, 0x6420);
-                    od[0] = __byte_perm(a.x, a.y, 0x7531);
-                    od[1] = __byte_perm(a.z, a.w, 0x7531);
-                } else {
-                    xplane[k * ng + g] = a;
-                }
-            }
-        }
+        // GS / 4 threads per group, four elements each, straight from global memory (the int4 group sums too)
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        quantize_to_planes<FMT == kQ4F16 ? 4 : 8, XM, GS, false, true>(p.x, n, reinterpret_cast<uint8_t *>(xplane),
+                                                                      sm.xs, sm.xsum, z, z, 0.0f);
     }
     __syncthreads();
-    if (FMT == kQ4F16) {
+    if (FMT == kQ4F16 && XM == kXQuantized) {  // the quantizing prologue wrote the group sums already
         for (int g = tid; g < ng; g += kThreads) {
             const uint4 e = xplane[g], o = xplane[ng + g];
             int s = __dp4a((int)e.x, 0x01010101, 0);

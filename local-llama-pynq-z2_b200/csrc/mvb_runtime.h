@@ -11,6 +11,11 @@ namespace mvb {
 void set_error(const char *fmt, ...) __attribute__((format(printf, 1, 2)));
 void clear_error();
 
+// The unique ID of the calling thread's current CUDA context (cuCtxGetId: never reused within a process, so a
+// context made after a cudaDeviceReset() has a new one), or 0 when there is no current context or the driver entry
+// points are missing. Caches of device addresses are keyed by it.
+unsigned long long current_context_id();
+
 // Validates and launches one matvec. fmt: WeightFormat; gs: 32 or 64; xmode: XMode. pdl: launch with
 // programmatic dependent launch. Returns 0, or -1 after set_error(). `who` prefixes messages.
 int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *ws, const void *xq, const void *xs,

@@ -94,10 +94,11 @@ __global__ void __launch_bounds__(kThreads) norm_quant_kernel(const float *x, co
     wait_for_producer();
     rmsnorm_smem(xb, sq, x, norm_w, n, eps);
     for (int g = threadIdx.x; g < n / 32; g += blockDim.x) {
-        int8_t q[32];
-        xs[g] = quantize_group<32>(xb, g, kXQuantizeQwen, q);
-#pragma unroll
-        for (int i = 0; i < 32; i++) xq[32 * g + i] = q[i];
+        uint32_t q4[8];
+        xs[g] = quantize_group<32>(xb, g, kXQuantizeQwen, q4);
+        uint4 *dst = reinterpret_cast<uint4 *>(xq + 32 * g);  // xq is 16-byte aligned
+        dst[0] = make_uint4(q4[0], q4[1], q4[2], q4[3]);
+        dst[1] = make_uint4(q4[4], q4[5], q4[6], q4[7]);
     }
     allow_consumer();
 }
@@ -148,6 +149,11 @@ struct Model {
     // the step again, with an event before every kernel and no programmatic overlap: per-kernel durations
     cudaGraphExec_t prof_graph = nullptr;
     std::vector<cudaEvent_t> prof_ev;
+    // the step again as the graph runs it (programmatic overlap included), every kernel stamping %globaltimer
+    // into its two slots of `stamps` (stamp_start / stamp_end): where the step's time goes, kernel by kernel
+    cudaGraphExec_t stamp_graph = nullptr;
+    unsigned long long *stamps = nullptr;
+    bool stamping = false;  // set while the stamped copy is captured
     struct Info { const char *kind; int layer; };
     std::vector<Info> info;  // one per kernel of the step, in launch order
     // batched prefill buffers (allocated on first use): up to `cap` tokens per batch
@@ -195,6 +201,7 @@ template <int BITS, int FAM, int GS, int EPI, int PRO, int TAIL, int UPT>
 static cudaError_t launch_decode(Model &m, DecodeParams p, int *count) {
     const size_t smem = decode_smem_bytes(p.n, GS, p.rt, EPI, PRO, TAIL, p.d);
     p.counter = m.counters + *count;
+    p.stamp = m.stamping ? m.stamps + 2 * *count : nullptr;
     (*count)++;
     return launch(decode_matvec_kernel<BITS, FAM, GS, EPI, PRO, TAIL, UPT>, dim3((p.d + p.rt - 1) / p.rt),
                   dim3(kThreads), smem, m.stream, m.pdl, p);
@@ -256,7 +263,8 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
     const int dim = c.dim, hid = c.hidden_dim, kv = m.kv_dim, L = c.n_layers;
     if ((e = mark("embed", -1)) != cudaSuccess) return e;
     e = launch(embed_kernel<FAM>, dim3((dim + kThreads - 1) / kThreads), dim3(kThreads), 0, m.stream, m.pdl,
-               (const int8_t *)m.emb.w, m.emb.s, m.x, dim, GS, m.st);
+               (const int8_t *)m.emb.w, m.emb.s, m.x, dim, GS, m.st,
+               m.stamping ? m.stamps + 2 * *count : (unsigned long long *)nullptr);
     (*count)++;
     if (e != cudaSuccess || (e = snap(0)) != cudaSuccess) return e;
     for (int l = 0; l < L; l++) {
@@ -280,6 +288,7 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
         a.kcache = m.kcache + (size_t)l * m.ctx * kv; a.vcache = m.vcache + (size_t)l * m.ctx * kv;
         a.xb = m.xb; a.dim = dim; a.kv_dim = kv; a.kv_mul = c.n_heads / c.n_kv_heads; a.ctx = m.ctx; a.st = m.st;
         a.et = m.et;
+        a.stamp = m.stamping ? m.stamps + 2 * *count : nullptr;
         if ((e = mark("attention", l)) != cudaSuccess || (e = launch_attention<FAM>(m, a)) != cudaSuccess) return e;
         (*count)++;
         // o: quantize the attention output in every CTA, x += wo * it
@@ -362,10 +371,11 @@ static void destroy(Model *m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->prof_graph) cudaGraphExecDestroy(m->prof_graph);
+    if (m->stamp_graph) cudaGraphExecDestroy(m->stamp_graph);
     for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     if (m->ring) cudaFreeHost(m->ring);
     void *bufs[] = {m->image, m->x, m->xb, m->qkv, m->hb, m->logits, m->kcache, m->vcache, m->rope, m->xq_n,
-                    m->xs_n, m->counters, m->prompt, m->ids, m->st, m->pf.x, m->pf.qkv, m->pf.qb, m->pf.att,
+                    m->xs_n, m->counters, m->prompt, m->ids, m->st, m->stamps, m->pf.x, m->pf.qkv, m->pf.qb, m->pf.att,
                     m->pf.out, m->pf.h1, m->pf.h3, m->pf.xs, m->pf.xq};
     for (void *b : bufs)
         if (b) cudaFree(b);
@@ -483,16 +493,18 @@ namespace mvb {
 namespace decode {
 
 // Captures one forward step into m->graph, then the instrumented copy (events between kernels, no programmatic
-// overlap) into m->prof_graph, replacing any earlier capture. Nothing of the model may be in flight.
+// overlap) into m->prof_graph and the stamped copy (the step as it runs, every kernel stamping the global timer)
+// into m->stamp_graph, replacing any earlier capture. Nothing of the model may be in flight.
 static cudaError_t capture_graphs(Model *m) {
     cudaError_t e;
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->prof_graph) cudaGraphExecDestroy(m->prof_graph);
-    m->graph = m->prof_graph = nullptr;
+    if (m->stamp_graph) cudaGraphExecDestroy(m->stamp_graph);
+    m->graph = m->prof_graph = m->stamp_graph = nullptr;
     for (cudaEvent_t ev : m->prof_ev) cudaEventDestroy(ev);
     m->prof_ev.clear();
     m->info.clear();
-    for (int pass = 0; pass < 2; pass++) {
+    for (int pass = 0; pass < 3; pass++) {
         cudaGraph_t graph;
         int count = 0;
         const bool pdl = m->pdl;
@@ -502,14 +514,16 @@ static cudaError_t capture_graphs(Model *m) {
             for (auto &ev : m->prof_ev)
                 if ((e = cudaEventCreate(&ev)) != cudaSuccess) return e;
         }
+        m->stamping = pass == 2;
         if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess) return e;
         cudaError_t le = pass == 0 ? enqueue_step(*m, &count, nullptr, &m->info)
-                                   : enqueue_step(*m, &count, m->prof_ev.data(), nullptr);
+                                   : enqueue_step(*m, &count, pass == 1 ? m->prof_ev.data() : nullptr, nullptr);
         e = cudaStreamEndCapture(m->stream, &graph);
         m->pdl = pdl;
+        m->stamping = false;
         if (le != cudaSuccess) return le;
         if (e != cudaSuccess) return e;
-        e = cudaGraphInstantiate(pass == 0 ? &m->graph : &m->prof_graph, graph, 0);
+        e = cudaGraphInstantiate(pass == 0 ? &m->graph : (pass == 1 ? &m->prof_graph : &m->stamp_graph), graph, 0);
         cudaGraphDestroy(graph);
         if (e != cudaSuccess) return e;
         if (pass == 0) m->kernels_per_step = count;
@@ -540,7 +554,8 @@ static Model *finish_load(Model *m, const std::vector<float> &rope, const char *
         (e = cudaMalloc(&m->counters, (size_t)(5 * L + 2) * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->prompt, (size_t)m->ctx * 4)) != cudaSuccess ||
         (e = cudaMalloc(&m->ids, (size_t)m->ctx * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&m->st, sizeof(State))) != cudaSuccess)
+        (e = cudaMalloc(&m->st, sizeof(State))) != cudaSuccess ||
+        (e = cudaMalloc(&m->stamps, (size_t)(5 * L + 2) * 2 * sizeof(unsigned long long))) != cudaSuccess)
         return fail("buffers");
     if ((e = cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
         (e = cudaMemset(m->kcache, 0, kvbytes)) != cudaSuccess ||
@@ -1058,6 +1073,30 @@ extern "C" int mvb_qwen_profile(void *model, float *ms, int cap) {
     return m->kernels_per_step;
 }
 
+// Runs the stamped copy of the step once from the current state (which it advances like a normal step) and writes,
+// for every kernel k, us[2k] = when its first CTA got past its wait for kernel k - 1 and us[2k + 1] = when its last
+// CTA finished, in microseconds after the first kernel's start. Returns the kernel count, or -1.
+extern "C" int mvb_qwen_stamps(void *model, double *us, int cap) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !us || cap < 2 * m->kernels_per_step) return -1;
+    const size_t bytes = (size_t)m->kernels_per_step * 2 * sizeof(unsigned long long);
+    std::vector<unsigned long long> t(2 * (size_t)m->kernels_per_step);
+    cudaError_t e = cudaMemsetAsync(m->stamps, 0, bytes, m->stream);
+    if (e == cudaSuccess) e = cudaGraphLaunch(m->stamp_graph, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(t.data(), m->stamps, bytes, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) {
+        set_error("mvb_qwen_stamps: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    if (wait_stream(*m, "mvb_qwen_stamps", timeout_s())) return -1;
+    const unsigned long long t0 = ~t[0];
+    for (int k = 0; k < m->kernels_per_step; k++) {
+        us[2 * k] = (double)(long long)(~t[2 * k] - t0) * 1e-3;
+        us[2 * k + 1] = (double)(long long)(t[2 * k + 1] - t0) * 1e-3;
+    }
+    return m->kernels_per_step;
+}
+
 // One forward at (token, pos) launched directly (not from the graph), copying the residual stream x to `trace`
 // (host, (2 * n_layers + 1) * dim floats) after the embedding and after every attention and FFN block.
 extern "C" int mvb_qwen_trace(void *model, int token, int pos, float *trace) {
@@ -1130,14 +1169,21 @@ constexpr int kStaticNormMatvecMaxN = kMaxDim;  // 2048 columns
 static __device__ __align__(256) uint8_t g_norm_matvec_scratch[kStaticNormMatvecMaxN + kStaticNormMatvecMaxN / 32 * 4];
 
 static std::mutex g_scratch_mu;
-static std::map<int, uint8_t *> g_scratch_addr;  // device ordinal -> device address of the array
+// device address of the array in each CUDA context it was looked up in, keyed by the context's unique ID
+// (cuCtxGetId: never reused within a process, so the context a cudaDeviceReset() makes next gets a lookup of its own)
+static std::map<unsigned long long, uint8_t *> g_scratch_addr;
 
-// The array's device address on the current device, looked up once per device. Host code only has a stand-in
-// for the array's name; handing that to a kernel would read the wrong memory.
+// The array's device address in the current device's context, looked up once per context (in practice once per
+// device: every runtime call of a device uses its one primary context). Host code only has a stand-in for the
+// array's name; handing that to a kernel would read the wrong memory. Without a context ID (no driver entry
+// points), the address is looked up on every call, which allocates nothing either.
 static uint8_t *scratch_address(int dev) {
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    auto it = g_scratch_addr.find(dev);
-    if (it != g_scratch_addr.end()) return it->second;
+    unsigned long long id = current_context_id();
+    if (id) {
+        auto it = g_scratch_addr.find(id);
+        if (it != g_scratch_addr.end()) return it->second;
+    }
     void *p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_norm_matvec_scratch);
     if (e != cudaSuccess || !p) {
@@ -1145,7 +1191,8 @@ static uint8_t *scratch_address(int dev) {
                   cudaGetErrorString(e));
         return nullptr;
     }
-    g_scratch_addr[dev] = static_cast<uint8_t *>(p);
+    if (!id) id = current_context_id();  // the lookup made the device's context current if it was not yet
+    if (id) g_scratch_addr[id] = static_cast<uint8_t *>(p);
     return static_cast<uint8_t *>(p);
 }
 
@@ -1155,8 +1202,15 @@ static uint8_t *scratch_address(int dev) {
 extern "C" int mvb_norm_matvec4_static(const float *x, const float *norm_w, float eps, const void *w, const void *ws,
                                        float *out, int n, int d, int wbits, void *stream) {
     using namespace mvb::decode;
-    if (!x || !norm_w) {
+    // every argument is checked before anything is launched: a refused call leaves the shared scratch (which a
+    // call on another stream may be reading) and the output untouched
+    if (!x || !norm_w || !w || !ws || !out) {
         set_error("mvb_norm_matvec4_static: null pointer argument");
+        return -1;
+    }
+    if (((uintptr_t)x & 3) || ((uintptr_t)norm_w & 3) || ((uintptr_t)w & 15) || ((uintptr_t)ws & 1) ||
+        ((uintptr_t)out & 3)) {
+        set_error("mvb_norm_matvec4_static: misaligned pointer (w needs 16 bytes, ws 2, x, norm_w and out 4)");
         return -1;
     }
     if (wbits != 4 && wbits != 8) {

@@ -7,7 +7,7 @@ and forward() through oracle/oracle.py. Inputs follow the reference testbenches'
     random mantissa (or exponent field row % 31 for the "special" rows: zero, subnormals up to 65504),
     xq uniform in [-128, 127], xs uniform in [1e-3, 1e-1]; shapes of :141-147 (quick set, plus the two
     special-scale shapes).
-  * hls/matvec_tb.cpp:225-233, 261-265: int8 wq and xq uniform in [-128, 127], ws uniform in [1e-4, 2e-2],
+  * hls/matvec_tb.cpp:56-62, 90-93: int8 wq and xq uniform in [-128, 127], ws uniform in [1e-4, 2e-2],
     xs uniform in [1e-3, 1e-1]; the testbench shapes that keep the fixture small.
 Per-group int32 sums come from the reference too: matmul_cpu() over one group's columns with unit scales
 returns (float)isum exactly (|isum| < 2^24).

@@ -1,6 +1,6 @@
 """The C-ABI library without a GPU: it loads, exports every entry point include/*.h declares, and keeps the
-reference driver's error behaviour for calls made before fpga_open() (driver/matvec_fpga.cpp:163-166, 211-214,
-245-248). No compute call runs here."""
+reference driver's error behaviour for calls made before fpga_open() (driver/matvec_fpga.cpp:127-129,
+174-176, 208-210). No compute call runs here."""
 import ctypes as C
 import subprocess
 import sys
@@ -27,7 +27,7 @@ def test_exports_every_declared_symbol(mvb):
 
 def test_calls_before_open_fail(mvb):
     L = mvb.lib()
-    L.fpga_close()  # safe when nothing is open (reference cpp:272-280)
+    L.fpga_close()  # safe when nothing is open (reference cpp:235-243)
     assert mvb.fpga_matvec4(0, 0, 0, 0, 0, 896, 896, 4) == -1
     assert "fpga_open() not called" in mvb.last_error()
     assert mvb.fpga_matvec(0, 0, 0, 0, 0, 288, 288, 32) == -1
@@ -46,7 +46,7 @@ def test_open_without_gpu_fails_loudly(mvb):
 
 
 def test_bad_memidx_rejected(mvb):
-    # FPGA_MEMIDX is parsed like the reference (cpp:120-128) before any device is touched
+    # FPGA_MEMIDX is parsed like the reference (cpp:83-91) before any device is touched
     code = ("import sys; sys.path.insert(0, %r); from conftest import load_pkg; m = load_pkg(); "
             "rc = m.fpga_open(); print(rc, m.last_error())" % (ROOT + "/tests"))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,

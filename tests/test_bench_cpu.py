@@ -89,6 +89,13 @@ def test_reference_arm_line_keeps_the_contract():
     assert line["impl"] == "reference" and line["metric"] == base["metric"]
     assert line["unit"] == "tok/s" and line["higher_is_better"] is True and line["value"] > 0
     assert line["n_gpus"] == 1 and line["config"]["workload"]
+    # the same config object and step count as the decode line of bench.py's own arm
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert line["config"] == bench.decode_config(1)
+    assert line["steps"] == 1 and line["warmup"] == 1
     cb = line["cpu_baseline"]
     assert cb["kind"] == "reference" and cb["cores"] == os.cpu_count() and cb["value"] == line["value"] and cb["sample"]
     assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}

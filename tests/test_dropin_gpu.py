@@ -152,7 +152,7 @@ def test_fpga_abi_host_buffers(mvb):
             out = abuf[out_off:out_off + 4 * d].view(np.float32)
             ref = restatement.matvec_f16(w, ws, xq, xs, n, d, 4)
             assert np.array_equal(out.view(np.uint32), ref.view(np.uint32)), trial
-        # the reference driver's rejections (cpp:249-253) and addresses outside every buffer
+        # the reference driver's rejections (cpp:212-216) and addresses outside every buffer
         assert mvb.fpga_matvec4(wphys + 8, wphys + off_ws, aphys, aphys + xs_off, aphys + out_off, n, d, 4) == -1
         assert mvb.fpga_matvec4(wphys, wphys + off_ws, aphys, aphys + xs_off, aphys + out_off, 8224, d, 4) == -1
         assert mvb.fpga_matvec4(wphys, wphys + off_ws, aphys, aphys + xs_off, aphys + out_off, n, d, 3) == -1
@@ -162,3 +162,38 @@ def test_fpga_abi_host_buffers(mvb):
     finally:
         mvb.fpga_close()
         mvb.fpga_close()  # safe twice
+
+
+def test_fpga_matvec_any_int8_alignment(mvb):
+    """fpga_matvec (runq's int8 path) takes its int8 weights and activations at any byte address, as the reference
+    driver does (driver/matvec_fpga.cpp:178 checks no alignment): planes at odd offsets inside the fpga_alloc()
+    buffers give the restatement's result bit for bit, over repeated calls (the aligned device copy of a misaligned
+    weight range is made once). fp32 arrays off their 4-byte alignment are refused."""
+    restatement = __import__("oracle").Restatement()
+    assert mvb.fpga_open() == 0
+    try:
+        rng = np.random.default_rng(5)
+        for n, d, gs, wo, xo in ((288, 768, 32, 1, 3), (768, 288, 64, 7, 13), (2048, 96, 32, 3, 1)):
+            wq = rng.integers(-127, 128, (d, n), dtype=np.int8)
+            ws = rng.uniform(1e-3, 2e-2, d * n // gs).astype(np.float32)
+            off_ws = (wo + wq.nbytes + 63) & ~63
+            wbuf, wphys = mvb.fpga_alloc(off_ws + ws.nbytes)
+            wbuf[wo:wo + wq.nbytes] = wq.view(np.uint8).reshape(-1)
+            wbuf[off_ws:off_ws + ws.nbytes] = ws.view(np.uint8)
+            abuf, aphys = mvb.fpga_alloc(16384 + 4 * d)
+            xs_off, out_off = 8192 + 64, 12288
+            for trial in range(2):
+                x = rng.standard_normal(n).astype(np.float32)
+                xq, xs = restatement.quantize_runq(x, gs)
+                abuf[xo:xo + n] = xq.view(np.uint8)
+                abuf[xs_off:xs_off + xs.nbytes] = xs.view(np.uint8)
+                assert mvb.fpga_matvec(wphys + wo, wphys + off_ws, aphys + xo, aphys + xs_off, aphys + out_off,
+                                       n, d, gs) == 0, mvb.last_error()
+                out = abuf[out_off:out_off + 4 * d].view(np.float32)
+                ref = restatement.matvec_f32(wq, ws, xq, xs, n, d, gs)
+                assert np.array_equal(out.view(np.uint32), ref.view(np.uint32)), (n, d, gs, trial)
+        assert mvb.fpga_matvec(wphys + wo, wphys + off_ws + 2, aphys + xo, aphys + xs_off, aphys + out_off,
+                               n, d, gs) == -1
+        assert "4-byte aligned" in mvb.last_error()
+    finally:
+        mvb.fpga_close()

@@ -43,3 +43,12 @@ def test_no_alloc_head_path_matches_decode(tmp_path):
     big = torch.zeros(4096, device="cuda")
     assert mvb.norm_matvec4_static(big, big, 1e-6, w, ws, out, 4096, 4, 8) == -1
     assert "at most n = 2048" in mvb.last_error()
+    # refused pointers (checked before any launch): no output, or misaligned weights; the previous output stays
+    before = out.clone()
+    assert mvb.norm_matvec4_static(x, norm, np.float32(c["rms_eps"]), w, ws, None, dim, hk, 8) == -1
+    assert "null pointer" in mvb.last_error()
+    w_odd = torch.empty(w.numel() + 16, dtype=torch.uint8, device="cuda")[1:1 + w.numel()]
+    assert mvb.norm_matvec4_static(x, norm, np.float32(c["rms_eps"]), w_odd, ws, out, dim, hk, 8) == -1
+    assert "misaligned" in mvb.last_error()
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int32), before.view(torch.int32))
