@@ -214,7 +214,6 @@ enum Epilogue : int {
     kEpiResidual = 1,  // out[row] += v                                              (qwen.c:551, :565)
     kEpiSwiGLU = 2,    // tile = rows of w1 then the same rows of w3; out[row] = silu(g) * u   (qwen.c:558-562,
                        //                                                                      runq.c:588-596)
-    kEpiHead = 3,      // out[row] = v, plus the argmax key                 (qwen.c:571, 591-598; runq.c:843-854)
 };
 
 enum Prologue : int {
@@ -226,8 +225,6 @@ enum Prologue : int {
 enum Tail : int {
     kTailNone = 0,
     kTailNormQuant = 1,  // rmsnorm(out) + quantize into tail_xq/xs               (qwen.c:569-570)
-    kTailNextToken = 3,  // the prompt's next token, else head_ids[argmax] (qwen.c:677-683) or the argmax row
-                         // itself when there are no head_ids (runq.c:1006-1012)
 };
 
 struct DecodeParams {
@@ -252,7 +249,25 @@ struct DecodeParams {
     int *ids;
     int cap;
     unsigned long long *stamp;  // this kernel's two timing slots (stamp_start / stamp_end), or null
+    // bytes that a later kernel will stream (the head's weights), prefetched into L2 by this kernel's CTAs before
+    // they wait for the previous kernel, or null: the decode step leaves HBM mostly idle, so the head can be read
+    // from L2 instead of waiting on HBM when its turn comes
+    const uint8_t *l2_pf;
+    size_t l2_pf_bytes;
 };
+
+// Asks L2 to fetch [p, p + bytes) (p 16-byte aligned, bytes a multiple of 16): a hint, no data comes back.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// This CTA's share of an L2 prefetch of [base, base + bytes): one thread issues it in 64 KB pieces.
+__device__ __forceinline__ void prefetch_share_l2(const uint8_t *base, size_t bytes) {
+    if (!base || threadIdx.x != 0) return;
+    const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+    const size_t b0 = per * blockIdx.x, b1 = min(b0 + per, bytes & ~(size_t)15);
+    for (size_t o = b0; o < b1; o += 65536) prefetch_l2(base + o, (uint32_t)min((size_t)65536, b1 - o));
+}
 
 // Bytes of a decode matvec CTA's per-group activation scales and int4 offset sums, padded to 16 so that the
 // product rows after them are 16-byte aligned.
@@ -311,6 +326,7 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
                                  : ld_u16(static_cast<const uint16_t *>(sb) + idx);
         }
     }
+    prefetch_share_l2(p.l2_pf, p.l2_pf_bytes);
     // the rmsnorm weights this thread applies (constants), also before the wait
     float4 nw4[kNormPasses];
     if (PRO == kProNorm) norm_weights_for_planes<GS>(p.norm_w, n, nw4);
@@ -462,24 +478,6 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
             gv = __fmul_rn(gv, __frcp_rn(__fadd_rn(1.0f, expf_ref(-gv, p.et))));  // 1.0f / (...) of both
             p.out[row0 + tid] = __fmul_rn(gv, u);
         }
-    } else {  // kEpiHead
-        unsigned long long key = 0ull;
-        if (tid < rows) {
-            p.out[row0 + tid] = v;
-            const float c = v == 0.0f ? 0.0f : v;  // -0 ties with +0, as the reference's `>` sees them
-            const uint32_t b = __float_as_uint(c);
-            const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-            if (c == c) key = ((unsigned long long)ord << 32) | (uint32_t)(~(uint32_t)(row0 + tid));
-            // The reference's scan starts from logit 0 and only moves on a strict `>`: a NaN there wins whatever
-            // follows (qwen.c:591-598, runq.c:843-854). The all-ones key beats every ordered value and names row 0.
-            else if (row0 + tid == 0) key = ~0ull;
-        }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
-            key = o > key ? o : key;
-        }
-        if ((tid & 31) == 0 && key) atomicMax(&p.st->key, key);
     }
 
     // 5. the last CTA prepares the next kernel's input
@@ -491,12 +489,79 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     if (TAIL == kTailNormQuant) {
         for (int j = tid; j < p.d / 4; j += kThreads) reinterpret_cast<float4 *>(sm)[j] = ld_cg4(p.out + 4 * j);
         rmsnorm_quantize<FAM, GS>(sm, sm + p.d, p.tail_norm, p.eps, p.d, p.tail_xq, p.tail_xs);
-    } else if (TAIL == kTailNextToken && tid == 0) {
+    }
+    stamp_end(p.stamp);
+}
+
+// The head's argmax key of logit v of row `row`: (v as an order-preserving integer << 32) | ~row, so that the
+// largest key is the largest logit and, among equal logits, the first row, as the reference's scan with a strict
+// `>` keeps (qwen.c:591-598, runq.c:843-854). -0 ties with +0, as `>` sees them. A NaN logit never wins, except
+// at row 0: the scan starts from logit 0 and no comparison with a NaN succeeds, so a NaN there is the answer
+// whatever follows; its all-ones key beats every ordered value and names row 0.
+__device__ __forceinline__ unsigned long long head_key(float v, int row) {
+    const float c = v == 0.0f ? 0.0f : v;
+    const uint32_t b = __float_as_uint(c);
+    const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    if (c == c) return ((unsigned long long)ord << 32) | (uint32_t)(~(uint32_t)row);
+    return row == 0 ? ~0ull : 0ull;
+}
+
+// The head (qwen.c's trimmed Q8 head, qwen.c:571; runq.c's classifier, runq.c:611): logits of every row, their
+// argmax, and the next token (qwen.c:677-683: the prompt's next token, else head_ids[argmax]; runq.c:1006-1012: the
+// argmax row itself). Persistent like matvec_kernel: one CTA per resident slot, each owning a balanced block of
+// rows streamed in tiles of p.rt rows with the int8 input staged once; each thread keeps the best key of the rows it
+// folded, one atomicMax per warp publishes them, and the last CTA to finish picks the token. The head's weights
+// were prefetched into L2 during the last layer (DecodeParams::l2_pf of an earlier kernel), so the tiles stream
+// from L2.
+template <int FAM, int GS>
+__global__ void __launch_bounds__(kThreads, 4) head_kernel(const DecodeParams p) {
+    constexpr int FMT = FAM == kRunq ? kQ8F32 : kQ8F16;
+    constexpr int XC = GS / 16;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int n = p.n, ng = n / GS, tid = threadIdx.x;
+    const MatvecSmem<GS> sm(smem, ng);
+    MatvecParams mp = {};
+    mp.w = p.w[0];
+    mp.ws = p.ws[0];
+    mp.n = n;
+    mp.d = p.d;
+    mp.rt = p.rt;
+    int r0, r1;
+    cta_rows(p.d, blockIdx.x, gridDim.x, r0, r1);
+    wait_for_producer();
+    stamp_start(p.stamp);
+    // the int8 input (written by the previous kernel: L2 loads) into the chunk planes, and its scales
+    for (int c = tid; c < n / 16; c += kThreads) {
+        const int g = c / XC, k = c % XC;
+        sm.xplane[k * ng + g] = __ldcg(reinterpret_cast<const uint4 *>(p.xq) + c);
+    }
+    for (int g = tid; g < ng; g += kThreads) sm.xs[g] = __ldcg(p.xs + g);
+    __syncthreads();
+    unsigned long long key = 0ull;
+    for (int row0 = r0; row0 < r1; row0 += p.rt) {
+        stream_tile<FMT, GS>(mp, sm, row0, min(p.rt, r1 - row0), [&](int row, float v) {
+            p.out[row] = v;
+            const unsigned long long k = head_key(v, row);
+            key = k > key ? k : key;
+        });
+        __syncthreads();  // the next tile rewrites the product buffer
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+        key = o > key ? o : key;
+    }
+    if ((tid & 31) == 0 && key) atomicMax(&p.st->key, key);
+    if (!last_cta(p.counter)) {
+        stamp_end(p.stamp);
+        return;
+    }
+    if (tid == 0) {
         State *st = p.st;
         const int pos = st->pos;
-        const unsigned long long key = atomicAdd(&st->key, 0ull);
+        const unsigned long long best = atomicAdd(&st->key, 0ull);
         // no key cannot happen (a NaN logit 0 gives the all-ones key); kept as row 0, the reference's answer
-        const int row = key ? (int)(~(uint32_t)(key & 0xffffffffu)) : 0;
+        const int row = best ? (int)(~(uint32_t)(best & 0xffffffffu)) : 0;
         st->last_row = row;
         if (st->n_prompt >= 0) {
             int next;

@@ -10,8 +10,9 @@
 //     gate/up (fused matvec)    rmsnorm(x) -> quantize -> w1, w3 rows paired, SwiGLU -> hb    qwen.c:554-562
 //     down (fused matvec)       quantize(hb) -> w2, x += out; after the last layer its last  qwen.c:563-565,
 //                               CTA also does the final rmsnorm + quantize                   :569-570
-//   head (matvec)               Q8 head rows -> logits, block argmax -> atomicMax; its last  qwen.c:571, 591-598,
-//                               CTA picks the next token (prompt[pos+1], else head_ids[argmax]) :677-683
+//   head (persistent matvec)    Q8 head rows -> logits, argmax -> atomicMax; its last CTA   qwen.c:571, 591-598,
+//                               picks the next token (prompt[pos+1], else head_ids[argmax])  :677-683
+//                               (the last layer's qkv kernel prefetched the head into L2)
 // The step reads the token and the position from device memory, so the same graph serves every position and
 // a whole generation is the graph launched once per position with no host work in between. The prompt is fed
 // in batches instead (prefill_batch: tensor-core matmuls, prefill_kernels.cuh), which writes the same KV cache.
@@ -197,6 +198,17 @@ static int decode_rt(int target, int n, int gs, int upt, bool pair) {
     return target < lim ? target : lim;
 }
 
+// The head: a persistent grid of one CTA per resident slot (at most one per row), tiles of p.rt rows.
+template <int FAM, int GS>
+static cudaError_t launch_head(Model &m, DecodeParams p, int *count) {
+    const size_t smem = matvec_smem_bytes(p.n, GS, p.rt);
+    const int slots = resident_slots((const void *)head_kernel<FAM, GS>, smem);
+    p.counter = m.counters + *count;
+    p.stamp = m.stamping ? m.stamps + 2 * *count : nullptr;
+    (*count)++;
+    return launch(head_kernel<FAM, GS>, dim3(p.d < slots ? p.d : slots), dim3(kThreads), smem, m.stream, m.pdl, p);
+}
+
 template <int BITS, int FAM, int GS, int EPI, int PRO, int TAIL, int UPT>
 static cudaError_t launch_decode(Model &m, DecodeParams p, int *count) {
     const size_t smem = decode_smem_bytes(p.n, GS, p.rt, EPI, PRO, TAIL, p.d);
@@ -275,6 +287,13 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
         p.w[2] = m.wv[l].w; p.ws[2] = m.wv[l].s; p.rows[2] = kv;
         p.n = dim; p.d = dim + 2 * kv; p.rt = decode_rt(8, dim, GS, U1, false);
         p.src = m.x; p.norm_w = m.attn_norm + (size_t)l * dim; p.eps = c.rms_eps; p.out = m.qkv; p.st = m.st;
+        if (l == L - 1) {  // the head's weights and scales into L2 while the last layer runs
+            const uint8_t *hw = m.head.w, *hs = static_cast<const uint8_t *>(m.head.s);
+            const size_t wb = (size_t)m.head_rows * dim, sb = (size_t)m.head_rows * (dim / GS) * (FAM == kRunq ? 4 : 2);
+            const uint8_t *lo = hw < hs ? hw : hs, *hi = hw + wb > hs + sb ? hw + wb : hs + sb;
+            p.l2_pf = lo;
+            p.l2_pf_bytes = (size_t)(hi - lo);
+        }
         if ((e = mark("qkv", l)) != cudaSuccess ||
             (e = launch_decode<BITS, FAM, GS, kEpiStore, kProNorm, kTailNone, U1>(m, p, count)) != cudaSuccess)
             return e;
@@ -324,12 +343,10 @@ static cudaError_t enqueue_step_family(Model &m, int *count, cudaEvent_t *ev, st
     // head (qwen.c's trimmed Q8 head, or runq.c's classifier): logits + argmax; the last CTA picks the next token
     DecodeParams p = {};
     p.w[0] = m.head.w; p.ws[0] = m.head.s; p.rows[0] = m.head_rows;
-    p.n = dim; p.d = m.head_rows; p.rt = decode_rt(32, dim, GS, U4, false);
+    p.n = dim; p.d = m.head_rows; p.rt = 32;
     p.xq = m.xq_n; p.xs = m.xs_n; p.out = m.logits; p.st = m.st;
     p.prompt = m.prompt; p.head_ids = m.head_ids; p.ids = m.ids; p.cap = m.ctx;
-    if ((e = mark("head", -1)) != cudaSuccess ||
-        (e = launch_decode<8, FAM, GS, kEpiHead, kProQuantized, kTailNextToken, U4>(m, p, count)) != cudaSuccess)
-        return e;
+    if ((e = mark("head", -1)) != cudaSuccess || (e = launch_head<FAM, GS>(m, p, count)) != cudaSuccess) return e;
     if (ev) e = cudaEventRecordWithFlags(ev[*count], m.stream, cudaEventRecordExternal);
     return e;
 }
