@@ -10,7 +10,9 @@
  *   - w/wq and ws ranges are weights: uploaded on first use and then treated as read-only. Hosts write every
  *     weight before their first matvec (qwen.c:324-329, runq.c:359-366); a weight range rewritten after it was
  *     first used is not seen again.
- *   - xq and xs are uploaded on every call; out is copied back into the host buffer before the call returns.
+ *   - xq and xs are read from the host buffer on every call (they travel inside the kernel launch's parameters);
+ *     the kernel writes out straight into the host buffer before the call returns (the device addresses the
+ *     pinned buffer directly).
  * Every call is synchronous and waits at most MATVEC_TIMEOUT_S seconds (default 5, like the reference's
  * TIMEOUT_S, driver/matvec_fpga.cpp:34). After a call that timed out, every later matvec call returns -1 until
  * fpga_close(): that call's result copy may still be in flight. Not thread-safe, like the reference (one caller

@@ -7,9 +7,14 @@
 //   ap_done busy poll with TIMEOUT_S (run_kernel, cpp:157-171)  -> cudaEventQuery poll against a deadline
 // State is process-global and not thread-safe, like the reference's static globals (cpp:50-56).
 //
-// MATVEC_STATS=1 (environment, read by fpga_open) times every call: host time to enqueue, device time of the
-// activation upload, the kernel and the result download (CUDA events), and the wait for completion; fpga_close()
-// prints the means over the calls that uploaded no weights as one "matvec stats: {...}" JSON line on stderr.
+// A call is one kernel launch: xq/xs are read from the caller's pinned buffer on the host and travel inside the
+// launch's parameters (no upload copy), the kernel's last CTA copies the result rows into the caller's pinned buffer,
+// which the device addresses directly (no download copy), and the call returns once the stream's completion event
+// fires.
+//
+// MATVEC_STATS=1 (environment, read by fpga_open) times every call: host time to enqueue, device time of the kernel
+// (CUDA events), and the wait for completion; fpga_close() prints the means over the calls that uploaded no weights
+// as one "matvec stats: {...}" JSON line on stderr.
 #include <errno.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -31,6 +36,7 @@ struct Buffer {
     char *host;      // pinned host memory the caller writes and reads
     uint64_t dev;    // device twin (same size), what the caller passes as a "physical address"
     size_t size;
+    char *hdev;      // the pinned host memory as the device addresses it (kernels read and write it directly)
 };
 
 struct Stats {
@@ -50,7 +56,7 @@ struct Driver {
     // weight ranges whose device address is not 16-byte aligned (fpga_matvec accepts any int8 address, as the
     // reference does): an aligned device copy per range, made on first use, keyed by (address, length)
     std::map<std::pair<uint64_t, size_t>, void *> shadows;
-    int8_t *xstage = nullptr;                // aligned device staging for misaligned activations (MAX_N + scales)
+    unsigned *last = nullptr;                // the call kernel's last-CTA counter (device, back to 0 after every call)
     size_t total = 0;
     size_t limit = 0;                        // MATVEC_ALLOC_LIMIT, 0 = none
     double timeout_s = 5.0;                  // MATVEC_TIMEOUT_S, reference TIMEOUT_S (cpp:34)
@@ -183,40 +189,19 @@ int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t
         set_error("%s: weight upload failed: %s", who, cudaGetErrorString(cudaGetLastError()));
         return -1;
     }
-    cudaError_t e;
     if (drv.stats_on) cudaEventRecord(drv.stats.ev[0], drv.stream);
-    const void *xqdev = (const void *)xq;
-    if (xq & 15) {  // a misaligned int8 activation vector: staged at an aligned device address instead
-        e = cudaMemcpyAsync(drv.xstage, bq->host + (xq - bq->dev), n, cudaMemcpyHostToDevice, drv.stream);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync((void *)xs, bx->host + (xs - bx->dev), ng * 4, cudaMemcpyHostToDevice, drv.stream);
-        xqdev = drv.xstage;
-    } else if (bq == bx && xs >= xq && xs - xq <= 65536) {  // one copy when the scales sit just after the values
-        e = cudaMemcpyAsync((void *)xq, bq->host + (xq - bq->dev), xs + ng * 4 - xq, cudaMemcpyHostToDevice,
-                            drv.stream);
-    } else {
-        e = cudaMemcpyAsync((void *)xq, bq->host + (xq - bq->dev), n, cudaMemcpyHostToDevice, drv.stream);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync((void *)xs, bx->host + (xs - bx->dev), ng * 4, cudaMemcpyHostToDevice, drv.stream);
-    }
-    if (e != cudaSuccess) {
-        set_error("%s: activation upload failed: %s", who, cudaGetErrorString(e));
-        return -1;
-    }
     if (drv.stats_on) cudaEventRecord(drv.stats.ev[1], drv.stream);
-    if (launch_matvec(who, fmt, gs, wdev, (const void *)ws, xqdev, (const void *)xs, nullptr, (float *)out, n, d,
-                      kXQuantized, drv.stream) != 0)
-        return -1;
-    if (drv.stats_on) cudaEventRecord(drv.stats.ev[2], drv.stream);
-    e = cudaMemcpyAsync(bo->host + (out - bo->dev), (const void *)out, (size_t)d * 4, cudaMemcpyDeviceToHost,
-                        drv.stream);
-    if (e != cudaSuccess) {
-        set_error("%s: result download failed: %s", who, cudaGetErrorString(e));
-        return -1;
+    int rc = launch_matvec_call(who, fmt, gs, wdev, (const void *)ws,
+                                reinterpret_cast<const int8_t *>(bq->host + (xq - bq->dev)),
+                                reinterpret_cast<const float *>(bx->host + (xs - bx->dev)), (float *)out,
+                                reinterpret_cast<float *>(bo->hdev + (out - bo->dev)), drv.last, n, d, drv.stream);
+    if (rc) return -1;
+    if (drv.stats_on) {
+        cudaEventRecord(drv.stats.ev[2], drv.stream);
+        cudaEventRecord(drv.stats.ev[3], drv.stream);
     }
-    if (drv.stats_on) cudaEventRecord(drv.stats.ev[3], drv.stream);
     const double t_enq = drv.stats_on ? now_s() : 0.0;
-    const int rc = wait_done(who, n, d, arg, argname);
+    rc = wait_done(who, n, d, arg, argname);
     if (rc == 0 && drv.stats_on) {
         Stats &st = drv.stats;
         if (uploaded) {
@@ -277,7 +262,8 @@ extern "C" int fpga_open(void) {
     if ((err = cudaSetDevice(dev)) != cudaSuccess ||
         (err = cudaStreamCreateWithFlags(&drv.stream, cudaStreamNonBlocking)) != cudaSuccess ||
         (err = cudaEventCreateWithFlags(&drv.done, cudaEventDisableTiming)) != cudaSuccess ||
-        (err = cudaMalloc(&drv.xstage, kMaxN + kMaxN / 32 * 4)) != cudaSuccess) {
+        (err = cudaMalloc(&drv.last, sizeof(unsigned))) != cudaSuccess ||
+        (err = cudaMemset(drv.last, 0, sizeof(unsigned))) != cudaSuccess) {
         set_error("fpga: cannot open CUDA device %d: %s", dev, cudaGetErrorString(err));
         fpga_close();
         return -1;
@@ -310,8 +296,9 @@ extern "C" void *fpga_alloc_try(size_t bytes, uint64_t *phys) {
         return nullptr;
     }
     cudaSetDevice(drv.device);
-    void *h = nullptr, *d = nullptr;
-    cudaError_t e = cudaHostAlloc(&h, bytes, cudaHostAllocPortable);
+    void *h = nullptr, *d = nullptr, *hd = nullptr;
+    cudaError_t e = cudaHostAlloc(&h, bytes, cudaHostAllocPortable | cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(&hd, h, 0);
     if (e == cudaSuccess) e = cudaMalloc(&d, bytes);
     if (e == cudaSuccess) e = cudaMemsetAsync(d, 0, bytes, drv.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(drv.stream);
@@ -324,7 +311,7 @@ extern "C" void *fpga_alloc_try(size_t bytes, uint64_t *phys) {
         return nullptr;
     }
     memset(h, 0, bytes);
-    drv.bufs[(uint64_t)d] = Buffer{(char *)h, (uint64_t)d, bytes};
+    drv.bufs[(uint64_t)d] = Buffer{(char *)h, (uint64_t)d, bytes, (char *)hd};
     drv.total += bytes;
     *phys = (uint64_t)d;
     return h;
@@ -377,9 +364,9 @@ extern "C" void fpga_close(void) {
         const Stats &st = drv.stats;
         const double c = st.calls > 0 ? st.calls : 1;
         fprintf(stderr,
-                "matvec stats: {\"calls\": %.0f, \"us_per_call\": %.2f, \"host_enqueue_us\": %.2f, \"h2d_us\": %.2f, "
-                "\"kernel_us\": %.2f, \"d2h_us\": %.2f, \"completion_wait_us\": %.2f, \"calls_with_weight_upload\": "
-                "%.0f}\n",
+                "matvec stats: {\"calls\": %.0f, \"us_per_call\": %.2f, \"host_enqueue_us\": %.2f, "
+                "\"upload_us\": %.2f, \"kernel_us\": %.2f, \"event_us\": %.2f, \"completion_wait_us\": %.2f, "
+                "\"calls_with_weight_upload\": %.0f}\n",
                 st.calls, st.total_us / c, st.enqueue_us / c, st.h2d_us / c, st.kernel_us / c, st.d2h_us / c,
                 st.wait_us / c, st.upload_calls);
         for (cudaEvent_t e : st.ev)
@@ -393,8 +380,8 @@ extern "C" void fpga_close(void) {
     }
     for (auto &kv : drv.shadows) cudaFree(kv.second);
     drv.shadows.clear();
-    if (drv.xstage) cudaFree(drv.xstage);
-    drv.xstage = nullptr;
+    if (drv.last) cudaFree(drv.last);
+    drv.last = nullptr;
     drv.bufs.clear();
     drv.resident.clear();
     if (drv.done) cudaEventDestroy(drv.done);

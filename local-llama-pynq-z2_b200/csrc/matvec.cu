@@ -112,6 +112,17 @@ static cudaError_t launch(MatvecParams p, cudaStream_t stream, bool pdl) {
 
 static bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
 
+// Launches `kernel` with one argument by value (which may exceed 4 KB) on `grid` CTAs of kThreads.
+template <typename K, typename A>
+static cudaError_t cudaLaunchKernelEx_helper(K kernel, int grid, size_t smem, cudaStream_t stream, const A &arg) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    return cudaLaunchKernelEx(&cfg, kernel, arg);
+}
+
 int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *ws, const void *xq, const void *xs,
                   const float *x, float *out, int n, int d, int xmode, cudaStream_t stream, bool pdl) {
     const bool quantized = xmode == kXQuantized;
@@ -157,6 +168,58 @@ int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *w
                                      : launch<kQ8F32, 32, kXQuantizeRunq>(p, stream, pdl);
     else e = quantized ? launch<kQ8F32, 64, kXQuantized>(p, stream, pdl)
                        : launch<kQ8F32, 64, kXQuantizeRunq>(p, stream, pdl);
+    if (e != cudaSuccess) {
+        set_error("%s: kernel launch failed: %s", who, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+template <int FMT, int GS, int NMAX>
+static cudaError_t launch_call(const MatvecParams &p, const int8_t *xq_host, const float *xs_host, float *host_out,
+                               unsigned *done, cudaStream_t stream) {
+    CallArgs<NMAX, GS> a;
+    a.p = p;
+    a.host_out = host_out;
+    a.done = done;
+    memcpy(a.xq, xq_host, p.n);
+    memcpy(a.xs, xs_host, (size_t)(p.n / GS) * 4);
+    size_t smem = 0;
+    const int grid = row_layout((const void *)matvec_call_kernel<FMT, GS, NMAX>, p.n, GS, p.d, a.p.rt, smem);
+    return cudaLaunchKernelEx_helper(matvec_call_kernel<FMT, GS, NMAX>, grid, smem, stream, a);
+}
+
+int launch_matvec_call(const char *who, int fmt, int gs, const void *w, const void *ws, const int8_t *xq_host,
+                       const float *xs_host, float *out, float *host_out, unsigned *done, int n, int d,
+                       cudaStream_t stream) {
+    if (!((fmt == kQ8F32 && (gs == 32 || gs == 64)) || ((fmt == kQ4F16 || fmt == kQ8F16) && gs == 32)) || n <= 0 ||
+        n > kMaxN || n % gs || d <= 0 || !w || !ws || !out || !host_out || !done || !aligned(w, 16) ||
+        !aligned(ws, fmt == kQ8F32 ? 4 : 2) || !aligned(out, 4) || !aligned(host_out, 4)) {
+        set_error("%s: bad call (format %d, group size %d, n=%d, d=%d, or a null or misaligned pointer)", who, fmt, gs,
+                  n, d);
+        return -1;
+    }
+    MatvecParams p = {};
+    p.w = static_cast<const uint8_t *>(w);
+    p.ws = ws;
+    p.out = out;
+    p.n = n;
+    p.d = d;
+    p.xmode = kXQuantized;
+    const bool small = n <= kCallSmallN;
+    cudaError_t e;
+    if (fmt == kQ4F16)
+        e = small ? launch_call<kQ4F16, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
+                  : launch_call<kQ4F16, 32, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+    else if (fmt == kQ8F16)
+        e = small ? launch_call<kQ8F16, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
+                  : launch_call<kQ8F16, 32, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+    else if (gs == 32)
+        e = small ? launch_call<kQ8F32, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
+                  : launch_call<kQ8F32, 32, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+    else
+        e = small ? launch_call<kQ8F32, 64, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
+                  : launch_call<kQ8F32, 64, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
     if (e != cudaSuccess) {
         set_error("%s: kernel launch failed: %s", who, cudaGetErrorString(e));
         return -1;

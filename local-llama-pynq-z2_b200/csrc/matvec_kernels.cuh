@@ -458,7 +458,7 @@ __device__ __forceinline__ void cta_rows(int d, int b, int grid, int &r0, int &r
 // Persistent: one CTA per resident slot (or per row when d is smaller), each owning a balanced contiguous block of
 // rows that it streams in tiles of at most rt rows, with the activations staged once.
 template <int FMT, int GS, int XM>
-__global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_kernel(const MatvecParams p) {
+__device__ __forceinline__ void matvec_body(const MatvecParams &p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const MatvecSmem<GS> sm(smem, p.n / GS);
     // The activations may come from the kernel launched just before this one.
@@ -470,6 +470,49 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_
         stream_tile<FMT, GS>(p, sm, row0, min(p.rt, r1 - row0), [&](int row, float v) { p.out[row] = v; });
         __syncthreads();  // the next tile rewrites the product buffer
     }
+}
+
+template <int FMT, int GS, int XM>
+__global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_kernel(const MatvecParams p) {
+    matvec_body<FMT, GS, XM>(p);
+}
+
+// The drop-in driver's call (driver/matvec_fpga.h's fpga_matvec / fpga_matvec4, one synchronous call per matvec):
+// the int8 activations and their scales travel inside the launch's own parameters (no separate upload), and once
+// every CTA has stored its rows in p.out, the last CTA to finish copies the whole output into the caller's pinned
+// host buffer host_out with 16-byte stores (no separate download). done: a zeroed counter that this CTA resets.
+template <int NMAX, int GS>
+struct CallArgs {
+    MatvecParams p;
+    float *host_out;
+    unsigned *done;
+    alignas(16) int8_t xq[NMAX];
+    alignas(16) float xs[NMAX / GS];
+};
+
+template <int FMT, int GS, int NMAX>
+__global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value)
+    matvec_call_kernel(const __grid_constant__ CallArgs<NMAX, GS> a) {
+    MatvecParams p = a.p;
+    p.xq = a.xq;  // read straight from the launch's parameter space
+    p.xs = a.xs;
+    matvec_body<FMT, GS, kXQuantized>(p);
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();  // every CTA's rows are visible
+    const int d = p.d;
+    if ((((uintptr_t)a.host_out | (uintptr_t)p.out) & 15) == 0) {
+        for (int i = threadIdx.x; i < d / 4; i += kThreads)
+            reinterpret_cast<float4 *>(a.host_out)[i] = __ldcg(reinterpret_cast<const float4 *>(p.out) + i);
+        for (int i = d / 4 * 4 + threadIdx.x; i < d; i += kThreads) a.host_out[i] = __ldcg(p.out + i);
+    } else {
+        for (int i = threadIdx.x; i < d; i += kThreads) a.host_out[i] = __ldcg(p.out + i);
+    }
+    if (threadIdx.x == 0) *a.done = 0;
 }
 
 }  // namespace mvb
