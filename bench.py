@@ -690,9 +690,11 @@ def sharded_cases(rank, world, iters, warmup, dist):
     row-sharded in contiguous blocks (rows per rank = ceil(d / world), the last block padded), every rank ending the
     step with the whole fp32 output. Timed per step with CUDA events, max over ranks: the fused kernel that stores its
     rows into every rank's output over NVLink (mvb_gather_matvec4 at batch 1, mvb_gather_gemm4 at batch 32: the
-    reported number), the plain matvec/matmul of the shard alone, and (world > 1) the plain call followed by an NCCL
-    all-gather, with the all-gather alone. Every rank checks its gathered output bit for bit against the unsharded
-    matvec (or matmul) of the whole matrix, and the NCCL path's result against the fused one."""
+    reported number) and the plain matvec/matmul of the shard alone, each as `iters` calls captured in a CUDA graph
+    (device time, no host launch cost between calls) and as calls launched one by one from Python (`*_eager_us`);
+    and (world > 1) the plain call followed by an NCCL all-gather, with the all-gather alone, launched from Python.
+    Every rank checks its gathered output bit for bit against the unsharded matvec (or matmul) of the whole matrix,
+    and the NCCL path's result against the fused one."""
     import torch
     mvb = sys.modules.get("mvb") or load_pkg()
     peak, peak_kind = peaks()
@@ -704,16 +706,31 @@ def sharded_cases(rank, world, iters, warmup, dist):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def timed(fn):
+    def timed(fn, graph=False):
         for i in range(warmup):
             fn(i)
         sync()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(iters):
-            fn(i)
-        e1.record()
-        torch.cuda.synchronize()
+        if graph:  # iters calls captured once, replayed: device time without host launch gaps
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                for i in range(iters):
+                    fn(i)
+            g.replay()
+            sync()
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del g
+        else:
+            e0.record()
+            for i in range(iters):
+                fn(i)
+            e1.record()
+            torch.cuda.synchronize()
         t = e0.elapsed_time(e1) / 1000.0 / iters
         if dist:
             tt = torch.tensor([t], dtype=torch.float64, device="cuda")
@@ -782,8 +799,11 @@ def sharded_cases(rank, world, iters, warmup, dist):
             else:
                 fused = lambda i: g.gemm4(w[i % copies], sc[i % copies], xq32, xs32, n, m, m, bits)
                 plain = lambda i: mvb.gemm4(w[i % copies], sc[i % copies], xq32, xs32, part, n, rows, m, m, bits)
-            t_fused = timed(fused)
-            t_plain = timed(plain)
+            t_fused = timed(fused, graph=True)
+            t_plain = timed(plain, graph=True)
+            t_fused_eager = timed(fused)
+            t_plain_eager = timed(plain)
+            sync()
             fused(0)
             torch.cuda.synchronize()
             got = g.output().clone()
@@ -792,7 +812,8 @@ def sharded_cases(rank, world, iters, warmup, dist):
             line = {"shape": f"{d}x{n} Q{bits}", "batch": batch, "n_gpus": world, "rows_per_gpu": rows,
                     "us_per_step": round(t_fused * 1e6, 2), "GBps_total": round(total / t_fused / 1e9, 1),
                     "frac_of_aggregate_hbm": round(total / t_fused / 1e9 / (peak * world), 4),
-                    "shard_alone_us": round(t_plain * 1e6, 2)}
+                    "shard_alone_us": round(t_plain * 1e6, 2), "exchange_us": round((t_fused - t_plain) * 1e6, 2),
+                    "fused_eager_us": round(t_fused_eager * 1e6, 2), "shard_alone_eager_us": round(t_plain_eager * 1e6, 2)}
             if batch > 1:
                 line["tokens_per_s"] = round(batch / t_fused, 1)
             if dist and world > 1:
@@ -814,6 +835,8 @@ def sharded_cases(rank, world, iters, warmup, dist):
         torch.cuda.empty_cache()
     return {"collective": "fused peer stores over NVLink (mvb_gather_matvec4 at batch 1, mvb_gather_gemm4 at batch 32, "
                           "the reported us_per_step); NCCL all_gather_into_tensor after the plain call for comparison",
+            "timing": "us_per_step and shard_alone_us: iters calls in one CUDA graph (device time); *_eager_us and the "
+                      "NCCL figures: calls launched one by one from Python; max over ranks",
             "check": "every rank's gathered output equals the unsharded matvec/matmul of the whole matrix bit for bit "
                      "(and the NCCL path's)", "peak_per_gpu": peak, "peak_source": f"{peak_kind} hbm_gbs",
             "iters": iters, "results": results}

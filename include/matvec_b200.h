@@ -193,7 +193,9 @@ int mvb_gemm_status(void *stream);
  *
  * Set-up: mvb_gather_create on every rank (fills `handle`, mvb_gather_handle_size() bytes, with this rank's
  * CUDA IPC handle), exchange the handles (any host channel), then mvb_gather_connect with all ranks' handles in
- * rank order. Every rank must then make the same sequence of mvb_gather_matvec4 calls with the same n. */
+ * rank order. Every rank must then make the same sequence of mvb_gather_matvec4 calls with the same n. Every call
+ * has the same launch arguments (the call number lives on the device), so a sequence of calls may be captured in a
+ * CUDA graph and replayed on every rank. */
 int mvb_gather_handle_size(void);
 void *mvb_gather_create(int rank, int world, int rows, void *handle);  /* NULL on error */
 /* The same with room for `tokens` tokens per call (mvb_gather_gemm4); mvb_gather_create holds one. */
@@ -205,7 +207,9 @@ int mvb_gather_connect(void *gather, const void *handles);            /* 0, or -
  * next operation. The output is double-buffered: read each call's output before the call after next. 0, or -1. */
 int mvb_gather_matvec4(void *gather, const void *w, const void *ws, const void *xq, const void *xs, int n, int wbits,
                        void *stream);
-float *mvb_gather_output(void *gather);  /* device pointer of the last call's gathered output */
+/* Device pointer of the last completed call's gathered output (synchronous: reads the gather's call counter, which
+ * the kernels keep on the device, so that calls replayed from a CUDA graph count too). */
+float *mvb_gather_output(void *gather);
 
 /* The batched form: m <= tokens tokens (xq m x n int8 token-major, xs n/32 x ldx fp32 group-major, as in
  * mvb_gemm4) through this rank's shard on the tensor cores; the gathered output is token-major, m x (rows * world)

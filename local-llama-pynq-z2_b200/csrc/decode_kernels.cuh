@@ -469,14 +469,14 @@ __global__ void __launch_bounds__(kThreads) decode_matvec_kernel(const DecodePar
     } else if (EPI == kEpiResidual) {
         if (tid < rows) p.out[row0 + tid] = __fadd_rn(old, v);
     } else if (EPI == kEpiSwiGLU) {
-        __syncthreads();  // prod is reused for the fold values
-        if (tid < vrows) prod[tid] = v;
-        __syncthreads();
-        if (tid < rows) {
-            float gv = prod[tid];
-            const float u = prod[rows + tid];
-            gv = __fmul_rn(gv, __frcp_rn(__fadd_rn(1.0f, expf_ref(-gv, p.et))));  // 1.0f / (...) of both
-            p.out[row0 + tid] = __fmul_rn(gv, u);
+        // the tile's at most 16 gate rows and their up rows were folded by warp 0: lane r takes row r's up value
+        // from lane rows + r
+        if (tid < 32) {
+            const float u = __shfl_sync(0xffffffffu, v, (tid + rows) & 31);
+            if (tid < rows) {
+                const float gv = __fmul_rn(v, __frcp_rn(__fadd_rn(1.0f, expf_ref(-v, p.et))));  // 1.0f / (...)
+                p.out[row0 + tid] = __fmul_rn(gv, u);
+            }
         }
     }
 

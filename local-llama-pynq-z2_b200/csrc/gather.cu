@@ -18,7 +18,9 @@
 //
 // The gathered output is double-buffered by call parity: a rank may start call e + 1 (and write into a peer's
 // buffer) while that peer still reads the output of call e, but it cannot reach call e + 2 before the peer has
-// finished call e + 1's kernel, which its stream orders after its reads of call e's output.
+// finished call e + 1's kernel, which its stream orders after its reads of call e's output. The call number lives on
+// the device (each rank's kernel advances its own counter once every rank's rows have arrived), so every call has
+// the same launch arguments and a sequence of calls can be captured in a CUDA graph.
 //
 // The wait is bounded (kGatherWaitNs of globaltimer, and kGatherSpin polls); when it runs out (a peer never ran
 // its kernel) it sets the gather's error word, read by mvb_gather_error, and the kernel ends.
@@ -36,17 +38,19 @@ namespace mvb {
 constexpr int kMaxRanks = kMaxGatherRanks;
 constexpr long kGatherSpin = 1L << 26;
 constexpr unsigned long long kGatherWaitNs = 2000000000ull;
-// Head of each rank's buffer, before the two output buffers: [0] arrival counter, [1] error word, [2] CTA counter.
+// Head of each rank's buffer, before the two output buffers: [0] arrival counter, [1] error word, [2] CTA counter,
+// [3] completed calls.
 constexpr size_t kGatherHead = 256;
 
 struct GatherParams {
     MatvecParams mv;            // this rank's shard (mv.out unused)
-    float *out[kMaxRanks];      // every rank's gathered output of this call (own buffer included)
+    float *out[kMaxRanks];      // every rank's gathered output buffer 0 (own included); buffer 1 follows obuf later
+    size_t obuf;                // floats between a rank's two output buffers
     unsigned *arrive[kMaxRanks];  // every rank's arrival counter
     unsigned *done;             // this rank's CTA counter (back to 0 at the end of every call)
+    unsigned *calls;            // this rank's completed calls (output parity, arrival target)
     int *err;                   // this rank's error word
     int world, rank, rows;
-    unsigned target;            // this rank's arrival counter once every rank has signalled this call
 };
 
 // Relaxed add; the system-scope fence before the first of them makes the group a release. (A release add per
@@ -70,7 +74,8 @@ template <int FMT>
 __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) gather_matvec_kernel(const GatherParams gp) {
     extern __shared__ __align__(16) uint8_t smem[];
     const MatvecSmem<32> sm(smem, gp.mv.n / 32);
-    const size_t base = (size_t)gp.rank * gp.rows;
+    const unsigned call = *gp.calls;  // read by every CTA before the last one advances it
+    const size_t base = (size_t)gp.rank * gp.rows + (call & 1) * gp.obuf;
     stage_activations<FMT, 32, kXQuantized>(gp.mv, sm);
     int r0, r1;
     cta_rows(gp.rows, blockIdx.x, gridDim.x, r0, r1);
@@ -88,27 +93,29 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) gather_
     if (atomicAdd(gp.done, 1u) != gridDim.x - 1) return;
     // The last CTA of this rank: every CTA's rows are stored. Signal every rank, then wait for all of them.
     *gp.done = 0;
+    const unsigned target = (call + 1u) * (unsigned)gp.world;  // every rank's signal of this call
     fence_acq_rel_sys();
 #pragma unroll
     for (int q = 0; q < kMaxRanks; q++)
         if (q < gp.world) red_relaxed_sys(gp.arrive[q], 1u);
     const unsigned long long t0 = global_ns();
     for (long i = 0; i < kGatherSpin; i++) {
-        if ((int)(ld_relaxed_sys(gp.arrive[gp.rank]) - gp.target) >= 0) {
+        if ((int)(ld_relaxed_sys(gp.arrive[gp.rank]) - target) >= 0) {
             fence_acq_rel_sys();
+            *gp.calls = call + 1u;
             return;
         }
         if ((i & 63) == 63 && global_ns() - t0 > kGatherWaitNs) break;
     }
     atomicExch(gp.err, 1);
+    *gp.calls = call + 1u;
 }
 
 struct Gather {
     int rank = 0, world = 0, rows = 0, tokens = 1;
     uint8_t *mem = nullptr;        // [kGatherHead | output 0 | output 1], each output tokens x rows * world fp32
     std::vector<uint8_t *> peer;   // every rank's `mem`, mapped here (own included)
-    unsigned expected = 0;         // this rank's arrival counter at the end of the last call
-    unsigned calls = 0;
+    unsigned calls = 0;            // calls enqueued through this handle (whether an output exists yet)
 };
 
 static size_t out_bytes(const Gather *g) { return (size_t)g->tokens * g->rows * g->world * 4; }
@@ -204,18 +211,18 @@ extern "C" int mvb_gather_matvec4(void *gather, const void *w, const void *ws, c
     const void *kernel = wbits == 4 ? (const void *)gather_matvec_kernel<kQ4F16> : (const void *)gather_matvec_kernel<kQ8F16>;
     size_t smem = 0;
     const int grid = row_layout(kernel, n, 32, g->rows, p.rt, smem);
-    const size_t off = kGatherHead + (g->calls & 1) * out_bytes(g);
     for (int q = 0; q < g->world; q++) {
-        gp.out[q] = reinterpret_cast<float *>(g->peer[q] + off);
+        gp.out[q] = reinterpret_cast<float *>(g->peer[q] + kGatherHead);
         gp.arrive[q] = reinterpret_cast<unsigned *>(g->peer[q]);
     }
+    gp.obuf = out_bytes(g) / 4;
     unsigned *head = reinterpret_cast<unsigned *>(g->mem);
     gp.err = reinterpret_cast<int *>(head + 1);
     gp.done = head + 2;
+    gp.calls = head + 3;
     gp.world = g->world;
     gp.rank = g->rank;
     gp.rows = g->rows;
-    gp.target = g->expected + (unsigned)g->world;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (wbits == 4) gather_matvec_kernel<kQ4F16><<<grid, kThreads, smem, s>>>(gp);
     else gather_matvec_kernel<kQ8F16><<<grid, kThreads, smem, s>>>(gp);
@@ -224,7 +231,6 @@ extern "C" int mvb_gather_matvec4(void *gather, const void *w, const void *ws, c
         set_error("mvb_gather_matvec4: launch failed: %s", cudaGetErrorString(e));
         return -1;
     }
-    g->expected = gp.target;
     g->calls++;
     return 0;
 }
@@ -249,30 +255,33 @@ extern "C" int mvb_gather_gemm4(void *gather, const void *w, const void *ws, con
         return -1;
     }
     PeerTargets pt = {};
-    const size_t off = kGatherHead + (g->calls & 1) * out_bytes(g);
     for (int q = 0; q < g->world; q++) {
-        pt.out[q] = reinterpret_cast<float *>(g->peer[q] + off);
+        pt.out[q] = reinterpret_cast<float *>(g->peer[q] + kGatherHead);
         pt.arrive[q] = reinterpret_cast<unsigned *>(g->peer[q]);
     }
+    pt.obuf = out_bytes(g) / 4;
     unsigned *head = reinterpret_cast<unsigned *>(g->mem);
     pt.err = reinterpret_cast<int *>(head + 1);
     pt.done = head + 2;
+    pt.calls = head + 3;
     pt.world = g->world;
     pt.rank = g->rank;
     pt.col0 = g->rank * g->rows;
-    pt.target = g->expected + (unsigned)g->world;
     if (gemm_launch(w, ws, xq, xs, nullptr, n, g->rows, m, ldx, g->rows * g->world, wbits,
                     static_cast<cudaStream_t>(stream), &pt))
         return -1;
-    g->expected = pt.target;
     g->calls++;
     return 0;
 }
 
+// The output buffer of the last completed call, from the device's call counter (graph replays advance it without
+// the host seeing the calls): synchronous, so read it once the calls' stream has finished.
 extern "C" float *mvb_gather_output(void *gather) {
     Gather *g = static_cast<Gather *>(gather);
     if (!g || !g->calls) return nullptr;
-    return reinterpret_cast<float *>(g->mem + kGatherHead + ((g->calls - 1) & 1) * out_bytes(g));
+    unsigned done = 0;
+    if (cudaMemcpy(&done, g->mem + 12, 4, cudaMemcpyDeviceToHost) != cudaSuccess || !done) return nullptr;
+    return reinterpret_cast<float *>(g->mem + kGatherHead + ((done - 1) & 1) * out_bytes(g));
 }
 
 extern "C" int mvb_gather_error(void *gather, void *stream) {

@@ -405,6 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&empty[s]);
             }
         }
+        // this rank's completed calls: the output buffer of this call (parity) in every rank's gather
+        const unsigned call = GATHER ? *p.peers.calls : 0u;
         if (!failed() && row < p.d) {
             if (!GATHER) {
 #pragma unroll
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const size_t o = (size_t)(m0 + col0 + c) * p.ldo + p.peers.col0 + row;
 #pragma unroll
                         for (int r = 0; r < kMaxGatherRanks; r++)
-                            if (r < p.peers.world) p.peers.out[r][o] = acc[c];
+                            if (r < p.peers.world) p.peers.out[r][(call & 1) * p.peers.obuf + o] = acc[c];
                     }
             }
         }
@@ -434,6 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the last CTA of this rank: every CTA's rows are stored. Signal every rank (one system-scope fence, then
         // relaxed adds: a release), then wait, bounded, until every rank has signalled this call.
         *p.peers.done = 0;
+        const unsigned call = *p.peers.calls;
+        const unsigned target = (call + 1u) * (unsigned)p.peers.world;  // every rank's signal of this call
         fence_acq_rel_sys();
         for (int r = 0; r < kMaxGatherRanks; r++)
             if (r < p.peers.world)
@@ -442,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t i = 0;; i++) {
             unsigned v;
             asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.peers.arrive[p.peers.rank]) : "memory");
-            if ((int)(v - p.peers.target) >= 0) {
+            if ((int)(v - target) >= 0) {
                 fence_acq_rel_sys();
                 break;
             }
@@ -451,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
         }
+        *p.peers.calls = call + 1u;  // every other CTA read the old value before it was counted
     }
 }
 

@@ -38,17 +38,20 @@ int resident_slots(const void *kernel, size_t smem);
 int rows_per_tile(int n, int d);
 
 // Where a row-sharded matmul stores its rows and how it signals completion (gather.cu's protocol): every rank's
-// gathered output (token-major, ldo floats per token, this rank's rows at columns col0 ..), every rank's arrival
-// counter, this rank's CTA counter and error word, and the value this rank's arrival counter reaches once every
-// rank has signalled this call.
+// gathered output buffer 0 (token-major, ldo floats per token, this rank's rows at columns col0 ..; buffer 1 follows
+// obuf floats later), every rank's arrival counter, this rank's CTA counter, call counter and error word. The call
+// counter, kept on the device and advanced by the kernel itself, picks the output buffer (call parity) and the
+// arrival count that means every rank has signalled this call, so the launch's arguments are the same for every
+// call (a sequence of calls can be captured in a CUDA graph and replayed).
 constexpr int kMaxGatherRanks = 8;
 struct PeerTargets {
     float *out[kMaxGatherRanks];
+    size_t obuf;
     unsigned *arrive[kMaxGatherRanks];
     unsigned *done;
+    unsigned *calls;
     int *err;
     int world, rank, col0;
-    unsigned target;
 };
 
 // The tensor-core prefill matmul of gemm.cu (mvb_gemm4) with an output leading dimension: out[t * ldo + i]. With

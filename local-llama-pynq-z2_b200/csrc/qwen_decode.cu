@@ -212,6 +212,7 @@ static cudaError_t launch_head(Model &m, DecodeParams p, int *count) {
 template <int BITS, int FAM, int GS, int EPI, int PRO, int TAIL, int UPT>
 static cudaError_t launch_decode(Model &m, DecodeParams p, int *count) {
     const size_t smem = decode_smem_bytes(p.n, GS, p.rt, EPI, PRO, TAIL, p.d);
+    if (EPI == kEpiSwiGLU && p.rt > 16) return cudaErrorInvalidValue;  // the epilogue folds in one warp
     p.counter = m.counters + *count;
     p.stamp = m.stamping ? m.stamps + 2 * *count : nullptr;
     (*count)++;
