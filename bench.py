@@ -57,15 +57,18 @@ MATVEC_KINDS = ("qkv", "o_proj", "gate_up", "down", "head")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
 
 
+# the sources the decode step's kernels are compiled from (qwen_decode.cu and what it includes)
+DECODE_SOURCES = ("qwen_decode.cu", "decode_kernels.cuh", "matvec_kernels.cuh", "prefill_kernels.cuh", "expf_ref.h",
+                  "mvb_runtime.h")
+
+
 def kernel_sources_sha():
-    """Short hash of the library's kernel sources (csrc/*.cu, *.cuh, *.h): names the code an ncu capture covers."""
-    import glob
+    """Short hash of the decode step's kernel sources: names the code an ncu capture of the step covers."""
     import hashlib
     h = hashlib.sha256()
-    for f in sorted(glob.glob(os.path.join(PKG, "csrc", "*"))):
-        if f.endswith((".cu", ".cuh", ".h")):
-            h.update(os.path.basename(f).encode())
-            h.update(open(f, "rb").read())
+    for f in DECODE_SOURCES:
+        h.update(f.encode())
+        h.update(open(os.path.join(PKG, "csrc", f), "rb").read())
     return h.hexdigest()[:12]
 
 
