@@ -25,6 +25,9 @@ greedy decode. One step = 128 greedy tokens from the filled prompt cache (positi
   sharded    config 5 (row-sharded 131072x8192 Q4 and the 151936-row Q8 head, batch 1 and 32) over all N ranks with
              the all-gather fused into the kernel (mvb_gather_*), beside the plain matvec + NCCL all-gather, each
              gathered vector checked bit for bit against the unsharded matvec (or matmul) of the whole matrix.
+  runq, sweep, prefill_gemm   (rank 0 at N = 1) configs 1 and 2 (runq.c's stories15M / stories110M models decoded
+             on the device, runq.c's CPU build beside them) and config 4 (the isolated matvec at M = 1 and the
+             tensor-core matmul at M = 16 / 128 / 512, with bit-identity against per-token matvecs).
 Every decode step reads the 263.7 MB of weights of a token, more than the 126 MB L2, so no flush is needed.
 
 --impl reference times the reference's CPU implementation (oracle/_ref/qwen) on the same workload: K runs after
@@ -215,7 +218,7 @@ def read_traffic(kind):
     return value, src
 
 
-def step_roofline(dec, token, pos, reps=5):
+def step_roofline(dec, token, pos, reps=5, traffic=True):
     """Where the decode step's time goes, kernel kind by kernel kind, as the captured graph runs it: `reps` steps at
     (token, pos) with every kernel stamping the global timer (mvb_qwen_stamps). A kernel's time is its last CTA's
     end minus the previous kernel's (so the kinds partition the step, the kernel boundaries included); its
@@ -253,7 +256,8 @@ def step_roofline(dec, token, pos, reps=5):
     mv_bytes = sum(kinds[k]["bytes"] for k in MATVEC_KINDS if k in kinds)
     mv_us = sum(kinds[k]["us"] for k in MATVEC_KINDS if k in kinds)
     all_bytes = sum(k["bytes"] for k in kinds.values())
-    traffic, traffic_src = read_traffic(dom)
+    # the committed capture is of the Qwen decode's kernels; other models' steps run other instantiations
+    traffic, traffic_src = read_traffic(dom) if traffic else (None, "no capture of this model's kernels")
     return {"bound": "hbm", "kernel": f"decode_matvec_kernel ({dom})", "kind": dom, "achieved": round(achieved, 1),
             "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
             "traffic": traffic, "traffic_source": traffic_src, "bytes_per_launch": round(d["bytes"] / d["launches"]),
@@ -366,6 +370,9 @@ def our_arm(args, rank, world, local_rank):
         prefill["reference_prompt_s"] = ref_prompt_s
     if rank == 0 and world == 1 and not args.no_cpu_baseline and os.path.exists(REF_QWEN_B200):
         dropin = dropin_block(path, prompt, ids_first.tolist(), local_rank)
+    extra = {}
+    if rank == 0 and world == 1 and not args.no_extra:
+        extra = extra_blocks(args, mvb)
     sharded = None
     if not args.no_sharded:
         sharded = sharded_cases(rank, world, max(args.steps, 50), max(args.warmup, 3), dist)
@@ -378,8 +385,39 @@ def our_arm(args, rank, world, local_rank):
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 32,
                         "d2h_bytes_per_step": 4 * GEN + 32},
                 "gpu_launches": args.steps * GEN * cfg["kernels_per_step"], "clocks": clk, "prefill": prefill,
-                "dropin": dropin, "sharded": sharded}
+                "dropin": dropin, "sharded": sharded, **extra}
         print(json.dumps(line), flush=True)
+
+
+CONFIG4_MATVEC_SHAPES = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 65536, 8)]
+
+
+def extra_blocks(args, mvb):
+    """The other configs of the reference's benchmark, measured on one GPU beside the decode line (rank 0, N = 1):
+    configs 1 and 2 (runq.c's stories15M / stories110M models decoded on the device, with runq.c's CPU build timed
+    beside them) and config 4 (the isolated matvec at M = 1 and the tensor-core matmul at M = 16 / 128 / 512)."""
+    import argparse as ap
+    import torch
+    ns = ap.Namespace(model="", gs=32, steps=max(1, min(args.steps, 10)), warmup=max(1, min(args.warmup, 3)),
+                      no_cpu_baseline=args.no_cpu_baseline)
+    keep = ("metric", "value", "unit", "us_per_token", "steps", "flushed", "e2e", "cpu_baseline", "kernels_per_token")
+    runq = []
+    for l in runq_results(ns):
+        r = {k: l[k] for k in keep}
+        r["workload"] = l["config"]["workload"]
+        r["stamped_step_us"] = l["roofline"]["stamped_step_us"]
+        runq.append(r)
+    peak, peak_kind = peaks()
+    sweep = sweep_results(mvb, torch, CONFIG4_MATVEC_SHAPES, [])
+    gemm, int8_peak = prefill_results(mvb, torch, PREFILL_SHAPES, (16, 128, 512), time_matvecs=False)
+    return {"runq": {"how": "configs 1 and 2 (bench.py --mode runq, fewer steps); value = device tok/s with the "
+                            "weights warm in L2, flushed = each token after a 256 MB L2 flush", "results": runq},
+            "sweep": {"how": "config 4 at M = 1: one matvec per call in a CUDA graph, weights rotated past L2; "
+                             "GB/s of the algorithmic bytes", "peak": peak, "peak_source": f"{peak_kind} hbm_gbs",
+                      "results": sweep},
+            "prefill_gemm": {"how": "config 4 at M = 16 / 128 / 512: the tcgen05 int8 matmul (mvb_gemm4) per call in "
+                                    "a CUDA graph, weights rotated past L2; same = equal bit for bit to one matvec "
+                                    "per token (M <= 128)", "int8_peak_TOPS": int8_peak, "results": gemm}}
 
 
 def dropin_block(path, prompt, ids_b200, gpu):
@@ -444,19 +482,12 @@ def _time_graph(torch, fn, reps):
     return statistics.median(times)
 
 
-def sweep_mode(args):
-    """Config 4: the isolated matvec at the Qwen2.5-0.5B layer shapes and the heads, plus the large sharded
-    matrix on one GPU; inputs rotate through copies larger than 2x L2 so every call reads HBM."""
-    import torch
-    mvb = load_pkg()
-    torch.cuda.set_device(0)
+def sweep_results(mvb, torch, shapes, runq_shapes, emit=False):
+    """The isolated matvec per shape (graph of calls, weights rotated past L2): runq's int8 fp32-scale matvec for
+    runq_shapes ((n, d), group size 32) and matvec4 for shapes ((n, d, bits), fp16 scales). Returns one dict per
+    shape (us, GB/s of the algorithmic bytes, fraction of the measured HBM peak)."""
     gen = torch.Generator(device="cuda").manual_seed(0)
-    peak, peak_kind = peaks()
-    shapes = SWEEP_SHAPES
-    runq_shapes = SWEEP_RUNQ_SHAPES  # runq's int8 weights with fp32 scales (fpga_matvec), group size 32
-    if args.only:
-        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
-        runq_shapes = [sh for sh in runq_shapes if f"{sh[1]}x{sh[0]}" == args.only]
+    peak, _ = peaks()
     out_lines = []
     for n, d in runq_shapes:
         gs = 32
@@ -472,7 +503,8 @@ def sweep_mode(args):
         line = {"shape": f"{d}x{n} Q8 fp32-scale (runq)", "us": round(t * 1e6, 3), "GBps": round(b / t / 1e9, 1),
                 "frac": round(b / t / 1e9 / peak, 4), "bytes": b, "copies": copies}
         out_lines.append(line)
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
         del w, sc
         torch.cuda.empty_cache()
     for n, d, bits in shapes:
@@ -488,9 +520,25 @@ def sweep_mode(args):
                 "frac": round(b / t / 1e9 / peak, 4), "bytes": b, "copies": copies,
                 "rows_per_tile": mvb.rows_per_tile(n, d)}
         out_lines.append(line)
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
         del w, sc
         torch.cuda.empty_cache()
+    return out_lines
+
+
+def sweep_mode(args):
+    """Config 4: the isolated matvec at the Qwen2.5-0.5B layer shapes and the heads, plus the large sharded
+    matrix on one GPU; inputs rotate through copies larger than 2x L2 so every call reads HBM."""
+    import torch
+    mvb = load_pkg()
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    shapes, runq_shapes = SWEEP_SHAPES, SWEEP_RUNQ_SHAPES
+    if args.only:
+        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+        runq_shapes = [sh for sh in runq_shapes if f"{sh[1]}x{sh[0]}" == args.only]
+    out_lines = sweep_results(mvb, torch, shapes, runq_shapes, emit=True)
     print(json.dumps({"mode": "sweep", "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "results": out_lines}))
 
 
@@ -568,32 +616,22 @@ def reference_sweep(args):
                                 "weights rotated through >= 512 MB of copies", "results": results}))
 
 
-def prefill_mode(args):
-    """Config 4's batched part: the tensor-core prefill matmul (mvb_gemm4) with M = 16, 128 and 512 tokens on the
-    Qwen2.5-0.5B layer shapes and the Q8 head, beside the same tokens as M calls of the matvec kernel (one per
-    token, as the reference prefills). Weights rotate through copies larger than 2x L2. Reported per shape and M:
-    us per call, int8 tensor ops 2*M*d*n per second against the int8 dense rate taken as twice the measured bf16
-    peak (B200's int8 rate is twice its bf16 rate), weight GB/s, and the epilogue's rate of group results
-    (M*d*n/32 per second); `same` says the GEMM's output equals the M matvecs' bit for bit."""
-    import torch
-    mvb = load_pkg()
-    torch.cuda.set_device(0)
+def prefill_results(mvb, torch, shapes, ms, time_matvecs=True, emit=False):
+    """The tensor-core matmul (mvb_gemm4) per shape ((n, d, bits)) and token count in ms (graph of calls, weights
+    rotated past L2), with `same`: its output equals one matvec4 call per token, bit for bit (M <= 128), and, when
+    time_matvecs, those M matvec calls timed too. Returns one dict per (shape, M)."""
     gen = torch.Generator(device="cuda").manual_seed(0)
-    peak, peak_kind = peaks()
     bf16 = 1590.0
     mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(mp):
         bf16 = float(json.load(open(mp)).get("bf16_tflops", bf16))
     int8_peak = 2 * bf16
-    shapes = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 65536, 8)]
-    if args.only:
-        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
     out_lines = []
     for n, d, bits in shapes:
         wb = d * n * bits // 8 + d * (n // 32) * 2
         copies = max(2, min(4096, -(-300 * 2**20 // wb)))
         w, sc = _rand_matrix(torch, n, d, bits, copies, gen)
-        for m in ([args.m] if args.m else (16, 128, 512)):
+        for m in ms:
             xq = torch.randint(-127, 128, (m, n), dtype=torch.int8, device="cuda", generator=gen)
             ldx = (m + 3) // 4 * 4
             xs = torch.rand((n // 32, ldx), device="cuda", generator=gen) * 0.05
@@ -611,7 +649,7 @@ def prefill_mode(args):
                 for tk in range(m):
                     mvb.matvec4(w[i % copies], sc[i % copies], xq[tk], xs_tok[tk], out_mv[tk], n, d, bits)
 
-            t_mv = _time_graph(torch, per_token, mv_reps) if m <= 128 else None
+            t_mv = _time_graph(torch, per_token, mv_reps) if m <= 128 and time_matvecs else None
             mvb.gemm4(w[0], sc[0], xq, xs, out, n, d, m, ldx, bits)
             per_token(0) if m <= 128 else None
             torch.cuda.synchronize()
@@ -623,9 +661,32 @@ def prefill_mode(args):
                     "matvecs_us": round(t_mv * 1e6, 2) if t_mv else None,
                     "speedup_vs_matvecs": round(t_mv / t, 1) if t_mv else None, "same": same, "status": status}
             out_lines.append(line)
-            print(json.dumps(line), flush=True)
+            if emit:
+                print(json.dumps(line), flush=True)
         del w, sc
         torch.cuda.empty_cache()
+    return out_lines, int8_peak
+
+
+PREFILL_SHAPES = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 65536, 8)]
+
+
+def prefill_mode(args):
+    """Config 4's batched part: the tensor-core prefill matmul (mvb_gemm4) with M = 16, 128 and 512 tokens on the
+    Qwen2.5-0.5B layer shapes and the Q8 head, beside the same tokens as M calls of the matvec kernel (one per
+    token, as the reference prefills). Weights rotate through copies larger than 2x L2. Reported per shape and M:
+    us per call, int8 tensor ops 2*M*d*n per second against the int8 dense rate taken as twice the measured bf16
+    peak (B200's int8 rate is twice its bf16 rate), weight GB/s, and the epilogue's rate of group results
+    (M*d*n/32 per second); `same` says the GEMM's output equals the M matvecs' bit for bit."""
+    import torch
+    mvb = load_pkg()
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    shapes = PREFILL_SHAPES
+    if args.only:
+        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+    mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    out_lines, int8_peak = prefill_results(mvb, torch, shapes, [args.m] if args.m else (16, 128, 512), emit=True)
     print(json.dumps({"mode": "prefill", "int8_peak_TOPS": int8_peak,
                       "peak_source": f"2 x {peak_kind} bf16_tflops" if os.path.exists(mp) else "2 x fallback bf16",
                       "results": out_lines}))
@@ -891,7 +952,7 @@ print(",".join(map(str, ids)))
     return float(out[0]), [int(t) for t in out[1].split(",") if t]
 
 
-def runq_mode(args):
+def runq_results(args):
     """Configs 1 and 2: runq.c's int8 models (stories15M / stories110M architectures, synthetic seeded weights,
     group size --gs (32, as the configs state; 64 is what tools/bin2q80.py gives stories110M), shared classifier)
     decoded on the device (mvb_runq_load + the captured step graph). One step = the rest
@@ -910,6 +971,7 @@ def runq_mode(args):
     names = [args.model] if args.model else list(RUNQ_MODELS)
     peak, peak_kind = peaks()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    lines = []
     for name in names:
         cfg_name, arch = RUNQ_MODELS[name]
         cfg = getattr(qwb, cfg_name)
@@ -966,7 +1028,7 @@ def runq_mode(args):
         stop = ids_ref.tolist().index(1) if 1 in ids_ref.tolist() else gen
         if ids.tolist() != ids_ref.tolist()[:stop]:
             raise RuntimeError("generate disagrees with the decode steps")
-        roof = step_roofline(dec, int(ids_ref[gen // 2 - 1]), pos0 + gen // 2)
+        roof = step_roofline(dec, int(ids_ref[gen // 2 - 1]), pos0 + gen // 2, traffic=False)
         kernels = dec.cfg["kernels_per_step"]
         dec.close()
         cpu = None
@@ -993,6 +1055,12 @@ def runq_mode(args):
                         "d2h_bytes_per_step": 4 * gen + 32, "includes": "prompt feed (3 positions)"},
                 "roofline": roof, "cpu_baseline": cpu, "gpu_launches": args.steps * gen * kernels,
                 "kernels_per_token": kernels, "load_s": round(load_s, 3), "clocks": clk}
+        lines.append(line)
+    return lines
+
+
+def runq_mode(args):
+    for line in runq_results(args):
         print(json.dumps(line), flush=True)
 
 
@@ -1004,6 +1072,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="decode: leave out the sharded (config 5) block")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="decode: leave out the runq (configs 1-2), sweep and prefill_gemm (config 4) blocks")
     ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
     ap.add_argument("--model", default="", choices=["", *RUNQ_MODELS], help="runq: only this model")
