@@ -213,3 +213,31 @@ def test_qwen05b_blocks_bit_exact_at_pos0(qwen05b):
         q3, s3 = rq.quantize(hb)
         x2 = tr[2 * l + 1] + mm(M.mats["w2"][l], q3, s3, hid, dim)
         assert np.array_equal(tr[2 * l + 2].view(np.uint32), x2.view(np.uint32)), f"ffn block {l}"
+
+
+def test_step_stamps_partition_the_step(tmp_path):
+    """mvb_qwen_stamps: one step as the graph runs it, every kernel stamping the global timer. Each kernel's first
+    CTA gets past its wait no earlier than the previous kernel's last CTA ends (the programmatic dependency), every
+    kernel ends after it starts, and the stamped step leaves the cache as a plain step would."""
+    import torch
+    mvb = load_pkg()
+    z = golden("qwen_tiny.npz")
+    path = str(tmp_path / "stamps_tiny.qwb")
+    mvb.qwb.write_synthetic_qwb(path, mvb.qwb.QWEN_TINY, seed=int(z["seed"]))
+    dec = mvb.QwenDecoder(path, ctx=64)
+    try:
+        seq = [int(t) for t in z["prompt"]] + [int(t) for t in z["ids"]]
+        row_plain, _ = dec.forward(seq[0], 0)
+        dec.rewind(seq[0], 0, -1)
+        st = dec.stamps()
+        assert st.shape == (dec.cfg["kernels_per_step"], 2)
+        assert st[0, 0] == 0.0  # times are relative to the first kernel's start
+        assert np.all(st[:, 1] >= st[:, 0])
+        assert np.all(st[1:, 0] >= st[:-1, 1] - 0.05)  # 50 ns of timer granularity
+        assert st[-1, 1] < 1e4  # a tiny model's step takes well under 10 ms
+        # the stamped step is the same step: a plain step repeated after it picks the same head row
+        dec.rewind(seq[0], 0, -1)
+        row_again, _ = dec.forward(seq[0], 0)
+        assert row_again == row_plain
+    finally:
+        dec.close()

@@ -4,8 +4,10 @@ share every host-side instruction; only the matvec backend differs. The bar is b
 position and identical greedy token ids.
 
 Needs oracle/_ref/ (built where the reference tree is available; it travels with the working tree)."""
+import json
 import os
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -197,3 +199,35 @@ def test_fpga_matvec_any_int8_alignment(mvb):
         assert "4-byte aligned" in mvb.last_error()
     finally:
         mvb.fpga_close()
+
+
+def test_fpga_stats_line():
+    """MATVEC_STATS=1: fpga_close() prints the mean per-call split as one JSON line on stderr, over the calls that
+    uploaded no weights (here: five calls on resident weights after the first, which uploads them)."""
+    code = r"""
+import sys, numpy as np
+sys.path.insert(0, %(root)r)
+from conftest import load_pkg
+mvb = load_pkg()
+assert mvb.fpga_open() == 0
+n, d = 896, 896
+wbuf, wphys = mvb.fpga_alloc(d * n // 2 + d * 28 * 2 + 64)
+rng = np.random.default_rng(0)
+wbuf[: d * n // 2] = rng.integers(0, 256, d * n // 2, dtype=np.uint8)
+off = (d * n // 2 + 63) & ~63
+wbuf[off: off + d * 56] = np.full(d * 28, 0x2000, np.uint16).view(np.uint8)
+abuf, aphys = mvb.fpga_alloc(8192)
+abuf[:n] = rng.integers(-128, 128, n, dtype=np.int8).view(np.uint8)
+abuf[1024: 1024 + 112] = np.full(28, 0.01, np.float32).view(np.uint8)
+for _ in range(6):
+    assert mvb.fpga_matvec4(wphys, wphys + off, aphys, aphys + 1024, aphys + 2048, n, d, 4) == 0
+mvb.fpga_close()
+""" % dict(root=os.path.join(ROOT, "tests"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, MATVEC_STATS="1"))
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = [l for l in r.stderr.splitlines() if l.startswith("matvec stats: ")]
+    assert len(line) == 1, r.stderr[-2000:]
+    stats = json.loads(line[0][len("matvec stats: "):])
+    assert stats["calls"] == 5 and stats["calls_with_weight_upload"] == 1
+    assert stats["us_per_call"] > 0 and stats["kernel_us"] > 0

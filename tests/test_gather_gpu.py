@@ -238,3 +238,36 @@ def test_gather_two_gpus():
         assert "error" not in results[r], results[r]
         assert all(v for k, v in results[r].items()), results[r]
     assert results[0]["timeout_reported"]
+
+
+def test_gather_graph_replay_one_rank(mvb, restatement):
+    """The fused gather keeps its call number on the device, so calls captured in a CUDA graph replay correctly:
+    after the graph of three calls is replayed twice (six calls, alternating output buffers), the output the
+    library reports is the last call's and equals the restatement bit for bit."""
+    import torch
+    torch.cuda.set_device(0)
+    n, d, bits = 896, 2048, 4
+    rng = np.random.default_rng(99)
+    w, ws = _random_q(rng, n, d, bits)
+    g = mvb.ShardGather(0, 1, d)
+    try:
+        g.connect([g.handle()])
+        wd, wsd = torch.from_numpy(w).cuda(), torch.from_numpy(ws.view(np.int16)).cuda()
+        xq, xs = _inputs(rng, n)
+        xqd, xsd = torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda()
+        g.matvec4(wd, wsd, xqd, xsd, n, bits)  # one eager call first
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(3):
+                g.matvec4(wd, wsd, xqd, xsd, n, bits)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        assert g.error() == 0
+        assert _same_bits(g.output().cpu().numpy(), restatement.matvec_f16(w, ws, xq, xs, n, d, bits))
+        del graph
+    finally:
+        g.close()
