@@ -53,20 +53,21 @@ unsigned long long current_context_id() {
 
 // Resident CTAs of `kernel` on the current device at kThreads threads and `smem` bytes (all SMs), cached per
 // device, kernel and size; 148 * 4 if the device cannot be queried.
-int resident_slots(const void *kernel, size_t smem) {
+int resident_slots(const void *kernel, size_t smem, int threads) {
     static std::mutex mu;
-    static std::map<std::tuple<int, const void *, size_t>, int> cache;
+    static std::map<std::tuple<int, const void *, size_t, int>, int> cache;
+    const int fallback = threads == kThreads ? 148 * 4 : 148;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 148 * 4;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fallback;
     std::lock_guard<std::mutex> lock(mu);
-    int &slots = cache[std::make_tuple(dev, kernel, smem)];
+    int &slots = cache[std::make_tuple(dev, kernel, smem, threads)];
     if (!slots) {
         int sms = 0, per_sm = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
             sms <= 0 || per_sm <= 0) {
             cudaGetLastError();
-            return 148 * 4;
+            return fallback;
         }
         slots = sms * per_sm;
     }

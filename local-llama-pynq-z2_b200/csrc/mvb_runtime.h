@@ -32,9 +32,10 @@ int launch_matvec_call(const char *who, int fmt, int gs, const void *w, const vo
                        cudaStream_t stream);
 
 // Persistent row layout of a matvec kernel (matvec_kernels.cuh): returns the grid, sets the tile rows and the
-// dynamic shared memory. resident_slots: resident CTAs of a kernel over all SMs of the current device.
+// dynamic shared memory. resident_slots: resident CTAs of a kernel (blocks of `threads`) over all SMs of the
+// current device.
 int row_layout(const void *kernel, int n, int gs, int d, int &rt, size_t &smem);
-int resident_slots(const void *kernel, size_t smem);
+int resident_slots(const void *kernel, size_t smem, int threads = 256);
 int rows_per_tile(int n, int d);
 
 // Where a row-sharded matmul stores its rows and how it signals completion (gather.cu's protocol): every rank's
