@@ -19,8 +19,8 @@
 //            (both 128-byte swizzled, the layout the MMA descriptors describe) and the tokens' scales of the
 //            block's four groups ([4][BN] fp32) into the next stage.
 //   warp 1   allocates tensor memory; one thread issues the MMAs: per k-block, D[slot][k] = A_k x B_k^T for its
-//            four groups into one of two TMEM slots of four BN-column group buffers, then one commit. MMAs run
-//            asynchronously, one k-block ahead of the epilogue.
+//            four groups into one of kSlots TMEM slots (4 for BN <= 32, else 2) of four BN-column group buffers,
+//            then one commit. MMAs run asynchronously, up to kSlots - 1 k-blocks ahead of the epilogue.
 //   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. For
 //            int4 weights they first unpack the packed tile of the k-block kStages/2 ahead into its int8
 //            operand tile (same swizzle), four 16-byte chunks per thread. Per k-block: tcgen05.ld of the
@@ -213,9 +213,11 @@ struct Smem {
     // four stages (measured: six to eight, which fit in shared memory, were slower: fewer resident CTAs)
     static constexpr int kStages = 4;
     static constexpr size_t kNatural = (size_t)kStages * kStage + 1024 /* align */ + 256 /* barriers */;
-    // TMEM: two k-block slots of four group buffers of BN columns. The shared memory request is raised so that no
-    // more CTAs than an SM's 512 columns hold can be resident (an allocation never has to wait).
-    static constexpr int kCols = 8 * BN < 32 ? 32 : 8 * BN;
+    // TMEM: kSlots k-block slots of four group buffers of BN columns (four slots where they fit, so the MMAs can
+    // run up to three k-blocks ahead of the epilogue). The shared memory request is raised so that no more CTAs
+    // than an SM's 512 columns hold can be resident (an allocation never has to wait).
+    static constexpr int kSlots = BN <= 32 ? 4 : 2;
+    static constexpr int kCols = kSlots * 4 * BN < 32 ? 32 : kSlots * 4 * BN;
     static constexpr size_t kFloor = 233472 / (512 / kCols + 1) + 1024;
     static constexpr size_t kBytes = kNatural > kFloor ? kNatural : kFloor;
     static_assert(kCols <= 512 && kBytes <= 232448, "tensor memory or shared memory per CTA");
@@ -251,9 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // full: the stage's copies landed. ready: its int4 tile is unpacked (8 epilogue warps). empty: the epilogue
     // has finished the stage's k-block (8 warps; its MMAs had completed before that). tfull / tempty: a TMEM
     // k-block slot was written (one commit) / has been read (8 warps).
+    constexpr int kSlots = S::kSlots;
     uint64_t *full = bar, *ready = bar + kStages, *empty = bar + 2 * kStages, *tfull = bar + 3 * kStages,
-             *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+             *tempty = tfull + kSlots;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + kSlots);
     constexpr int kCols = S::kCols;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -273,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&ready[s], kEpiWarps);
             mbar_init(&empty[s], kEpiWarps);
         }
-        for (int j = 0; j < 2; j++) {
+        for (int j = 0; j < kSlots; j++) {
             mbar_init(&tfull[j], 1);
             mbar_init(&tempty[j], kEpiWarps);
         }
@@ -326,15 +329,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- MMA issue: one thread ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_i8(kBM, BN);
-            int j = 0;  // this CTA's k-blocks issued so far (TMEM slot j & 1)
+            int j = 0;  // this CTA's k-blocks issued so far (TMEM slot j % kSlots)
             bool stop = false;
             for (int i = 0; i < mine && !stop; i++) {
                 for (int kb = 0; kb < nkb; kb++) {
-                    const int s = j % kStages, slot = j & 1;
+                    const int s = j % kStages, slot = j % kSlots;
                     if (!mbar_wait(&full[s], (j / kStages) & 1, kErrFullWait) ||
                         (BITS == 4 && !mbar_wait(&ready[s], (j / kStages) & 1, kErrRaw)) ||
                         // the slot's previous k-block must have been read by the epilogue
-                        (j >= 2 && !mbar_wait(&tempty[slot], ((j >> 1) - 1) & 1, kErrTmemEmpty))) {
+                        (j >= kSlots && !mbar_wait(&tempty[slot], ((j / kSlots) - 1) & 1, kErrTmemEmpty))) {
                         stop = true;
                         break;
                     }
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             // all MMAs complete before tensor memory is freed: wait (bounded) for the last commit
-            if (j > 0) mbar_wait(&tfull[(j - 1) & 1], ((j - 1) >> 1) & 1, kErrTmemFull);
+            if (j > 0) mbar_wait(&tfull[(j - 1) % kSlots], ((j - 1) / kSlots) & 1, kErrTmemFull);
         }
     } else {
         // ---------------- epilogue (and int4 unpack, kLag k-blocks ahead) ----------------
@@ -389,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint16_t *wsr = scales_of(row);
             const uint16_t *wsn = i + 1 < mine ? scales_of(row_of(i + 1)) : wsr;
             for (int kb = 0; kb < nkb; kb++, j++) {
-                const int s = j % kStages, slot = j & 1;
+                const int s = j % kStages, slot = j % kSlots;
                 if (BITS == 4 && j + kLag < total && !(ok = unpack(j + kLag))) break;
                 uint16_t wcur[4];
                 const bool last = kb + 1 == nkb;
@@ -401,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wnext[k] = g < ngroups ? __ldg((last ? wsn : wsr) + g) : (uint16_t)0;
                 }
                 if (!(ok = mbar_wait(&full[s], (j / kStages) & 1, kErrFullWait))) break;  // this stage's token scales
-                if (!(ok = mbar_wait(&tfull[slot], (j >> 1) & 1, kErrTmemFull))) break;
+                if (!(ok = mbar_wait(&tfull[slot], (j / kSlots) & 1, kErrTmemFull))) break;
                 tc_fence_after();
                 const float *xst = stage_x(s);
                 const int ng_kb = min(kBK / 32, ngroups - kb * (kBK / 32));
