@@ -4,13 +4,15 @@
 //                                                                 twin's device address
 //   AXI-Lite register writes + ap_start (fpga_matvec, cpp:173-199; fpga_matvec4, cpp:207-233)
 //                                                               -> argument validation, host<->HBM copies, launch
-//   ap_done busy poll with TIMEOUT_S (run_kernel, cpp:157-171)  -> cudaEventQuery poll against a deadline
+//   ap_done busy poll with TIMEOUT_S (run_kernel, cpp:157-171)  -> poll of a mapped completion word against a
+//                                                                 deadline
 // State is process-global and not thread-safe, like the reference's static globals (cpp:50-56).
 //
 // A call is one kernel launch: xq/xs are read from the caller's pinned buffer on the host and travel inside the
 // launch's parameters (no upload copy), the kernel's last CTA copies the result rows into the caller's pinned buffer,
-// which the device addresses directly (no download copy), and the call returns once the stream's completion event
-// fires.
+// which the device addresses directly (no download copy), then writes the call's number into a completion word in
+// mapped host memory, and the call returns once the host sees that number there (the stream is asked about errors
+// every 1024 polls).
 //
 // MATVEC_STATS=1 (environment, read by fpga_open) times every call: host time to enqueue, device time of the kernel
 // (CUDA events), and the wait for completion; fpga_close() prints the means over the calls that uploaded no weights
@@ -21,6 +23,7 @@
 #include <string.h>
 #include <time.h>
 
+#include <atomic>
 #include <map>
 #include <vector>
 
@@ -43,6 +46,8 @@ struct Stats {
     cudaEvent_t ev[4] = {};  // before the activation upload, before the launch, after the kernel, after the download
     double calls = 0, enqueue_us = 0, h2d_us = 0, kernel_us = 0, d2h_us = 0, wait_us = 0, total_us = 0;
     double upload_calls = 0;  // calls that also uploaded weights (first use), left out of the means
+    double between_us = 0;    // host time from the return of the previous call to the entry of this one
+    double t_return = 0;      // when the previous call returned (0: none yet)
 };
 
 struct Driver {
@@ -50,13 +55,16 @@ struct Driver {
     bool failed = false;                     // a call timed out: its copies may still land, so refuse further calls
     int device = 0;
     cudaStream_t stream = nullptr;
-    cudaEvent_t done = nullptr;
     std::map<uint64_t, Buffer> bufs;         // keyed by device base address
     std::map<uint64_t, uint64_t> resident;   // weight byte ranges [first, second) already uploaded (merged)
     // weight ranges whose device address is not 16-byte aligned (fpga_matvec accepts any int8 address, as the
     // reference does): an aligned device copy per range, made on first use, keyed by (address, length)
     std::map<std::pair<uint64_t, size_t>, void *> shadows;
     unsigned *last = nullptr;                // the call kernel's last-CTA counter (device, back to 0 after every call)
+    // the call's completion word: pinned host memory the kernel's last CTA writes the call's number into
+    volatile unsigned *flag = nullptr;
+    unsigned *flag_dev = nullptr;
+    unsigned seq = 0;
     size_t total = 0;
     size_t limit = 0;                        // MATVEC_ALLOC_LIMIT, 0 = none
     double timeout_s = 5.0;                  // MATVEC_TIMEOUT_S, reference TIMEOUT_S (cpp:34)
@@ -116,24 +124,36 @@ bool ensure_resident(const Buffer &b, uint64_t addr, size_t len, bool *uploaded)
 }
 
 // Waits for the stream's work with a deadline; 0, or -1 on timeout or a CUDA error.
-int wait_done(const char *who, int n, int d, int arg, const char *argname) {
-    cudaError_t e = cudaEventRecord(drv.done, drv.stream);
-    if (e != cudaSuccess) {
-        set_error("%s: %s", who, cudaGetErrorString(e));
-        return -1;
-    }
+int wait_done(const char *who, unsigned seq, int n, int d, int arg, const char *argname) {
+    // The kernel's last CTA writes seq into the mapped completion word after the output (a system-scope fence
+    // between them): polling that word sees the end of the call sooner than an event would. Every 1024 polls the
+    // stream is asked about errors and the deadline is checked.
     const double deadline = now_s() + drv.timeout_s;
     for (unsigned i = 1;; i++) {
-        e = cudaEventQuery(drv.done);
-        if (e == cudaSuccess) return 0;
-        if (e != cudaErrorNotReady) {
-            set_error("%s: device error: %s (n=%d d=%d %s=%d)", who, cudaGetErrorString(e), n, d, argname, arg);
-            return -1;
+        if (*drv.flag == seq) {
+            std::atomic_thread_fence(std::memory_order_acquire);  // the output is read after the word
+            return 0;
         }
-        if (i % 256 == 0 && now_s() > deadline) {
-            set_error("%s: kernel did not finish in %g s (n=%d d=%d %s=%d)", who, drv.timeout_s, n, d, argname, arg);
-            drv.failed = true;  // its result download is still queued: no later call may reuse the buffers
-            return -1;
+#if defined(__x86_64__) || defined(__i386__)
+        __builtin_ia32_pause();  // a polite spin: the core's other hardware thread keeps its issue slots
+#endif
+        if (i % 1024 == 0) {
+            const cudaError_t e = cudaStreamQuery(drv.stream);
+            if (e != cudaSuccess && e != cudaErrorNotReady) {
+                set_error("%s: device error: %s (n=%d d=%d %s=%d)", who, cudaGetErrorString(e), n, d, argname, arg);
+                return -1;
+            }
+            if (e == cudaSuccess && *drv.flag != seq) {
+                set_error("%s: the kernel ended without signalling completion (n=%d d=%d %s=%d)", who, n, d, argname,
+                          arg);
+                return -1;
+            }
+            if (now_s() > deadline) {
+                set_error("%s: kernel did not finish in %g s (n=%d d=%d %s=%d)", who, drv.timeout_s, n, d, argname,
+                          arg);
+                drv.failed = true;  // its output copy may still land: no later call may reuse the buffers
+                return -1;
+            }
         }
     }
 }
@@ -194,14 +214,15 @@ int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t
     int rc = launch_matvec_call(who, fmt, gs, wdev, (const void *)ws,
                                 reinterpret_cast<const int8_t *>(bq->host + (xq - bq->dev)),
                                 reinterpret_cast<const float *>(bx->host + (xs - bx->dev)), (float *)out,
-                                reinterpret_cast<float *>(bo->hdev + (out - bo->dev)), drv.last, n, d, drv.stream);
+                                reinterpret_cast<float *>(bo->hdev + (out - bo->dev)), drv.last, drv.flag_dev,
+                                ++drv.seq, n, d, drv.stream);
     if (rc) return -1;
     if (drv.stats_on) {
         cudaEventRecord(drv.stats.ev[2], drv.stream);
         cudaEventRecord(drv.stats.ev[3], drv.stream);
     }
     const double t_enq = drv.stats_on ? now_s() : 0.0;
-    rc = wait_done(who, n, d, arg, argname);
+    rc = wait_done(who, drv.seq, n, d, arg, argname);
     if (rc == 0 && drv.stats_on) {
         Stats &st = drv.stats;
         if (uploaded) {
@@ -211,6 +232,7 @@ int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t
             float ms[3] = {0, 0, 0};
             for (int i = 0; i < 3; i++) cudaEventElapsedTime(&ms[i], st.ev[i], st.ev[i + 1]);
             st.calls++;
+            if (st.t_return > 0) st.between_us += (t_entry - st.t_return) * 1e6;
             st.enqueue_us += (t_enq - t_entry) * 1e6;
             st.wait_us += (t_done - t_enq) * 1e6;
             st.total_us += (t_done - t_entry) * 1e6;
@@ -218,6 +240,7 @@ int run_call(const char *who, int fmt, int gs, uint64_t w, uint64_t ws, uint64_t
             st.kernel_us += ms[1] * 1e3;
             st.d2h_us += ms[2] * 1e3;
         }
+        st.t_return = now_s();
     }
     return rc;
 }
@@ -261,13 +284,17 @@ extern "C" int fpga_open(void) {
     }
     if ((err = cudaSetDevice(dev)) != cudaSuccess ||
         (err = cudaStreamCreateWithFlags(&drv.stream, cudaStreamNonBlocking)) != cudaSuccess ||
-        (err = cudaEventCreateWithFlags(&drv.done, cudaEventDisableTiming)) != cudaSuccess ||
         (err = cudaMalloc(&drv.last, sizeof(unsigned))) != cudaSuccess ||
-        (err = cudaMemset(drv.last, 0, sizeof(unsigned))) != cudaSuccess) {
+        (err = cudaMemset(drv.last, 0, sizeof(unsigned))) != cudaSuccess ||
+        (err = cudaHostAlloc((void **)&drv.flag, sizeof(unsigned), cudaHostAllocPortable | cudaHostAllocMapped)) !=
+            cudaSuccess ||
+        (err = cudaHostGetDevicePointer((void **)&drv.flag_dev, (void *)drv.flag, 0)) != cudaSuccess) {
         set_error("fpga: cannot open CUDA device %d: %s", dev, cudaGetErrorString(err));
         fpga_close();
         return -1;
     }
+    *drv.flag = 0;
+    drv.seq = 0;
     drv.stats_on = stats != 0;
     drv.stats = Stats{};
     for (int i = 0; drv.stats_on && i < 4; i++)
@@ -366,9 +393,9 @@ extern "C" void fpga_close(void) {
         fprintf(stderr,
                 "matvec stats: {\"calls\": %.0f, \"us_per_call\": %.2f, \"host_enqueue_us\": %.2f, "
                 "\"upload_us\": %.2f, \"kernel_us\": %.2f, \"event_us\": %.2f, \"completion_wait_us\": %.2f, "
-                "\"calls_with_weight_upload\": %.0f}\n",
+                "\"host_between_calls_us\": %.2f, \"calls_with_weight_upload\": %.0f}\n",
                 st.calls, st.total_us / c, st.enqueue_us / c, st.h2d_us / c, st.kernel_us / c, st.d2h_us / c,
-                st.wait_us / c, st.upload_calls);
+                st.wait_us / c, st.between_us / c, st.upload_calls);
         for (cudaEvent_t e : st.ev)
             if (e) cudaEventDestroy(e);
         drv.stats = Stats{};
@@ -384,9 +411,11 @@ extern "C" void fpga_close(void) {
     drv.last = nullptr;
     drv.bufs.clear();
     drv.resident.clear();
-    if (drv.done) cudaEventDestroy(drv.done);
+    if (drv.flag) cudaFreeHost((void *)drv.flag);
+    drv.flag = nullptr;
+    drv.flag_dev = nullptr;
+    drv.seq = 0;
     if (drv.stream) cudaStreamDestroy(drv.stream);
-    drv.done = nullptr;
     drv.stream = nullptr;
     drv.total = 0;
     drv.failed = false;

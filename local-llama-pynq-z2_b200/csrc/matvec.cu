@@ -176,25 +176,33 @@ int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *w
     return 0;
 }
 
+// The call's layout: one CTA per 32 rows, up to the resident slots (row_layout's one CTA per slot would have every
+// CTA of a small matrix stage the activations for one or two rows).
 template <int FMT, int GS, int NMAX>
 static cudaError_t launch_call(const MatvecParams &p, const int8_t *xq_host, const float *xs_host, float *host_out,
-                               unsigned *done, cudaStream_t stream) {
+                               unsigned *done, unsigned *flag, unsigned seq, cudaStream_t stream) {
     CallArgs<NMAX, GS> a;
     a.p = p;
     a.host_out = host_out;
     a.done = done;
+    a.flag = flag;
+    a.seq = seq;
     memcpy(a.xq, xq_host, p.n);
     memcpy(a.xs, xs_host, (size_t)(p.n / GS) * 4);
-    size_t smem = 0;
-    const int grid = row_layout((const void *)matvec_call_kernel<FMT, GS, NMAX>, p.n, GS, p.d, a.p.rt, smem);
-    return cudaLaunchKernelEx_helper(matvec_call_kernel<FMT, GS, NMAX>, grid, smem, stream, a);
+    const int slots = resident_slots((const void *)matvec_call_kernel<FMT, GS, NMAX>, matvec_smem_bytes(p.n, GS, 32));
+    const int tiles = (p.d + 31) / 32;
+    const int grid = tiles < slots ? tiles : slots;
+    const int per_cta = (p.d + grid - 1) / grid;
+    a.p.rt = per_cta < 32 ? per_cta : 32;
+    return cudaLaunchKernelEx_helper(matvec_call_kernel<FMT, GS, NMAX>, grid, matvec_smem_bytes(p.n, GS, a.p.rt),
+                                     stream, a);
 }
 
 int launch_matvec_call(const char *who, int fmt, int gs, const void *w, const void *ws, const int8_t *xq_host,
-                       const float *xs_host, float *out, float *host_out, unsigned *done, int n, int d,
-                       cudaStream_t stream) {
+                       const float *xs_host, float *out, float *host_out, unsigned *done, unsigned *flag,
+                       unsigned seq, int n, int d, cudaStream_t stream) {
     if (!((fmt == kQ8F32 && (gs == 32 || gs == 64)) || ((fmt == kQ4F16 || fmt == kQ8F16) && gs == 32)) || n <= 0 ||
-        n > kMaxN || n % gs || d <= 0 || !w || !ws || !out || !host_out || !done || !aligned(w, 16) ||
+        n > kMaxN || n % gs || d <= 0 || !w || !ws || !out || !host_out || !done || !flag || !aligned(w, 16) ||
         !aligned(ws, fmt == kQ8F32 ? 4 : 2) || !aligned(out, 4) || !aligned(host_out, 4)) {
         set_error("%s: bad call (format %d, group size %d, n=%d, d=%d, or a null or misaligned pointer)", who, fmt, gs,
                   n, d);
@@ -210,17 +218,17 @@ int launch_matvec_call(const char *who, int fmt, int gs, const void *w, const vo
     const bool small = n <= kCallSmallN;
     cudaError_t e;
     if (fmt == kQ4F16)
-        e = small ? launch_call<kQ4F16, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
-                  : launch_call<kQ4F16, 32, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+        e = small ? launch_call<kQ4F16, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, flag, seq, stream)
+                  : launch_call<kQ4F16, 32, kMaxN>(p, xq_host, xs_host, host_out, done, flag, seq, stream);
     else if (fmt == kQ8F16)
-        e = small ? launch_call<kQ8F16, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
-                  : launch_call<kQ8F16, 32, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+        e = small ? launch_call<kQ8F16, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, flag, seq, stream)
+                  : launch_call<kQ8F16, 32, kMaxN>(p, xq_host, xs_host, host_out, done, flag, seq, stream);
     else if (gs == 32)
-        e = small ? launch_call<kQ8F32, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
-                  : launch_call<kQ8F32, 32, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+        e = small ? launch_call<kQ8F32, 32, kCallSmallN>(p, xq_host, xs_host, host_out, done, flag, seq, stream)
+                  : launch_call<kQ8F32, 32, kMaxN>(p, xq_host, xs_host, host_out, done, flag, seq, stream);
     else
-        e = small ? launch_call<kQ8F32, 64, kCallSmallN>(p, xq_host, xs_host, host_out, done, stream)
-                  : launch_call<kQ8F32, 64, kMaxN>(p, xq_host, xs_host, host_out, done, stream);
+        e = small ? launch_call<kQ8F32, 64, kCallSmallN>(p, xq_host, xs_host, host_out, done, flag, seq, stream)
+                  : launch_call<kQ8F32, 64, kMaxN>(p, xq_host, xs_host, host_out, done, flag, seq, stream);
     if (e != cudaSuccess) {
         set_error("%s: kernel launch failed: %s", who, cudaGetErrorString(e));
         return -1;

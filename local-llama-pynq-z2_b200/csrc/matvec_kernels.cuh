@@ -480,12 +480,16 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value) matvec_
 // The drop-in driver's call (driver/matvec_fpga.h's fpga_matvec / fpga_matvec4, one synchronous call per matvec):
 // the int8 activations and their scales travel inside the launch's own parameters (no separate upload), and once
 // every CTA has stored its rows in p.out, the last CTA to finish copies the whole output into the caller's pinned
-// host buffer host_out with 16-byte stores (no separate download). done: a zeroed counter that this CTA resets.
+// host buffer host_out with 16-byte stores (no separate download), fences at system scope and writes the call's
+// number seq into the mapped host word flag, which the host polls instead of waiting for the stream. done: a
+// zeroed counter that this CTA resets.
 template <int NMAX, int GS>
 struct CallArgs {
     MatvecParams p;
     float *host_out;
     unsigned *done;
+    unsigned *flag;
+    unsigned seq;
     alignas(16) int8_t xq[NMAX];
     alignas(16) float xs[NMAX / GS];
 };
@@ -512,7 +516,12 @@ __global__ void __launch_bounds__(kThreads, MatvecMinBlocks<FMT>::value)
     } else {
         for (int i = threadIdx.x; i < d; i += kThreads) a.host_out[i] = __ldcg(p.out + i);
     }
-    if (threadIdx.x == 0) *a.done = 0;
+    __syncthreads();  // every thread's part of host_out is stored
+    if (threadIdx.x == 0) {
+        *a.done = 0;
+        __threadfence_system();
+        *reinterpret_cast<volatile unsigned *>(a.flag) = a.seq;
+    }
 }
 
 }  // namespace mvb

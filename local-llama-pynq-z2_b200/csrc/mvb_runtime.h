@@ -23,13 +23,14 @@ int launch_matvec(const char *who, int fmt, int gs, const void *w, const void *w
 
 // One synchronous-style call of the drop-in driver (fpga_matvec / fpga_matvec4): activations xq_host (n int8) and
 // xs_host (n/gs fp32) in host memory are copied into the launch's parameters; the kernel writes its rows to `out`
-// (device) and its last CTA copies them to host_out (pinned host memory the device addresses). done: a zeroed device
-// counter (the kernel resets it). Inputs up to kCallSmallN columns travel in a 1 KB parameter block, larger ones in a
-// kMaxN one. 0, or -1 after set_error().
+// (device) and its last CTA copies them to host_out (pinned host memory the device addresses), then writes seq into
+// the mapped host word flag (device address), after a system-scope fence. done: a zeroed device counter (the kernel
+// resets it). Inputs up to kCallSmallN columns travel in a 1 KB parameter block, larger ones in a kMaxN one. 0, or
+// -1 after set_error().
 constexpr int kCallSmallN = 1024;
 int launch_matvec_call(const char *who, int fmt, int gs, const void *w, const void *ws, const int8_t *xq_host,
-                       const float *xs_host, float *out, float *host_out, unsigned *done, int n, int d,
-                       cudaStream_t stream);
+                       const float *xs_host, float *out, float *host_out, unsigned *done, unsigned *flag,
+                       unsigned seq, int n, int d, cudaStream_t stream);
 
 // Persistent row layout of a matvec kernel (matvec_kernels.cuh): returns the grid, sets the tile rows and the
 // dynamic shared memory. resident_slots: resident CTAs of a kernel (blocks of `threads`) over all SMs of the
