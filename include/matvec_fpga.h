@@ -16,8 +16,11 @@
  * Every call is synchronous and waits at most MATVEC_TIMEOUT_S seconds (default 5, like the reference's
  * TIMEOUT_S, driver/matvec_fpga.cpp:34). After a call that timed out, every later matvec call returns -1 until
  * fpga_close(): that call's result copy may still be in flight. Not thread-safe, like the reference (one caller
- * thread). MATVEC_STATS=1 makes fpga_close() print the mean per-call times (host enqueue, upload, kernel,
- * download, completion wait) as one "matvec stats: {...}" line on stderr.
+ * thread). A call returns when the kernel's last CTA has written the call's number into a completion word in
+ * mapped host memory (after the output, with a system-scope fence between); the host polls that word and asks
+ * the stream about errors every 1024 polls. MATVEC_STATS=1 makes fpga_close() print the mean per-call times
+ * (host enqueue, upload, kernel, download, completion wait, host time between calls) as one "matvec stats: {...}"
+ * line on stderr.
  */
 #ifndef MATVEC_FPGA_H
 #define MATVEC_FPGA_H
