@@ -685,6 +685,9 @@ def prefill_mode(args):
     shapes = PREFILL_SHAPES
     if args.only:
         shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
+        m = re.fullmatch(r"(\d+)x(\d+)(?:q([48]))?", args.only)
+        if not shapes and m:  # a shape outside config 4 (rows x columns, Q4 unless qN follows), e.g. 8192x8192
+            shapes = [(int(m.group(2)), int(m.group(1)), int(m.group(3) or 4))]
     mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     out_lines, int8_peak = prefill_results(mvb, torch, shapes, [args.m] if args.m else (16, 128, 512), emit=True)
     print(json.dumps({"mode": "prefill", "int8_peak_TOPS": int8_peak,
@@ -1074,7 +1077,8 @@ def main():
     ap.add_argument("--no-sharded", action="store_true", help="decode: leave out the sharded (config 5) block")
     ap.add_argument("--no-extra", action="store_true",
                     help="decode: leave out the runq (configs 1-2), sweep and prefill_gemm (config 4) blocks")
-    ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896)")
+    ap.add_argument("--only", default="", help="sweep, prefill: run only this shape, rows x columns (e.g. 4864x896); "
+                                               "prefill also takes any shape, Q4 unless qN follows (8192x8192, 65536x896q8)")
     ap.add_argument("--m", type=int, default=0, help="prefill: run only this token count")
     ap.add_argument("--model", default="", choices=["", *RUNQ_MODELS], help="runq: only this model")
     ap.add_argument("--full-head", action="store_true", help="step: the full-vocabulary head (mvb_qwen_full_head)")

@@ -248,7 +248,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kStages = S::kStages;
     constexpr int kLag = kStages / 2;  // k-blocks the epilogue warps unpack ahead of the one they finish (int4)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // aligned to 1024 bytes by an offset added to the shared array itself: a pointer that went through an integer
+    // cast would be generic, and every stage access through it a generic load or store
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * S::kStage);
     // full: the stage's copies landed. ready: its int4 tile is unpacked (8 epilogue warps). empty: the epilogue
     // has finished the stage's k-block (8 warps; its MMAs had completed before that). tfull / tempty: a TMEM

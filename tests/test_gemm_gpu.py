@@ -62,6 +62,37 @@ def test_gemm_matches_matvec_per_token(mvb, torch, restatement, n, d, m, bits):
     assert _same_bits(out, _expect(restatement, w, ws, xq, xs, n, d, m, bits))
 
 
+@pytest.mark.parametrize("n,d,m,bits", [(896, 20000, 128, 8), (896, 19456, 100, 4), (1024, 40000, 16, 8)])
+def test_gemm_persistent_tiles(mvb, torch, restatement, n, d, m, bits):
+    """More tiles than one wave (one CTA per SM walking several tiles, the pipeline running on from one tile into
+    the next; the last shape runs one CTA per tile with two CTAs per SM): every token's row bit-identical too."""
+    rng = np.random.default_rng(d + m + bits)
+    w, ws, xq, xs = _random_case(rng, n, d, m, bits)
+    out = _run(mvb, torch, w, ws, xq, xs, n, d, m, bits)
+    assert _same_bits(out, _expect(restatement, w, ws, xq, xs, n, d, m, bits))
+
+
+def test_gemm_scales_two_byte_aligned(mvb, torch, restatement):
+    """Weight scales that start 2 bytes past an 8-byte boundary (the launcher accepts any even address): the
+    epilogue reads them one by one instead of four at a time, with the same results."""
+    rng = np.random.default_rng(77)
+    n, d, m, bits = 896, 1000, 40, 4
+    w, ws, xq, xs = _random_case(rng, n, d, m, bits)
+    ng = n // 32
+    ldx = (m + 3) // 4 * 4
+    xs_gm = np.zeros((ng, ldx), np.float32)
+    xs_gm[:, :m] = xs.T
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    buf = torch.zeros(d * ng + 4, dtype=torch.int16, device="cuda")
+    wsd = buf[1:1 + d * ng]
+    wsd.copy_(dev(ws.view(np.int16).reshape(-1)))
+    assert wsd.data_ptr() % 8 == 2
+    out = torch.full((m, d), float("nan"), device="cuda")
+    mvb.gemm4(dev(w), wsd, dev(xq), dev(xs_gm), out, n, d, m, ldx, bits)
+    assert mvb.gemm_status() == 0
+    assert _same_bits(out.cpu().numpy(), _expect(restatement, w, ws, xq, xs, n, d, m, bits))
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 def test_gemm_every_scale_pattern_and_extreme_sums(mvb, torch, restatement, bits):
     rng = np.random.default_rng(5 + bits)
