@@ -671,6 +671,19 @@ def prefill_results(mvb, torch, shapes, ms, time_matvecs=True, emit=False):
 PREFILL_SHAPES = [(896, 896, 4), (896, 128, 4), (896, 4864, 4), (4864, 896, 4), (896, 65536, 8)]
 
 
+def prefill_shapes(only):
+    """The (columns, rows, bits) shapes of --mode prefill: config 4's, the one of them named by `only` (rows x
+    columns), or any shape `only` names outside them (rows x columns, Q4 unless qN follows: 8192x8192, 65536x896q8);
+    [] for a name that is neither."""
+    if not only:
+        return list(PREFILL_SHAPES)
+    shapes = [sh for sh in PREFILL_SHAPES if f"{sh[1]}x{sh[0]}" == only]
+    m = re.fullmatch(r"(\d+)x(\d+)(?:q([48]))?", only)
+    if not shapes and m:
+        shapes = [(int(m.group(2)), int(m.group(1)), int(m.group(3) or 4))]
+    return shapes
+
+
 def prefill_mode(args):
     """Config 4's batched part: the tensor-core prefill matmul (mvb_gemm4) with M = 16, 128 and 512 tokens on the
     Qwen2.5-0.5B layer shapes and the Q8 head, beside the same tokens as M calls of the matvec kernel (one per
@@ -682,12 +695,7 @@ def prefill_mode(args):
     mvb = load_pkg()
     torch.cuda.set_device(0)
     peak, peak_kind = peaks()
-    shapes = PREFILL_SHAPES
-    if args.only:
-        shapes = [sh for sh in shapes if f"{sh[1]}x{sh[0]}" == args.only]
-        m = re.fullmatch(r"(\d+)x(\d+)(?:q([48]))?", args.only)
-        if not shapes and m:  # a shape outside config 4 (rows x columns, Q4 unless qN follows), e.g. 8192x8192
-            shapes = [(int(m.group(2)), int(m.group(1)), int(m.group(3) or 4))]
+    shapes = prefill_shapes(args.only)
     mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     out_lines, int8_peak = prefill_results(mvb, torch, shapes, [args.m] if args.m else (16, 128, 512), emit=True)
     print(json.dumps({"mode": "prefill", "int8_peak_TOPS": int8_peak,

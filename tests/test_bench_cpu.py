@@ -108,3 +108,18 @@ def test_reference_arm_other_ranks_exit_quietly():
                        capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_prefill_shapes_by_name():
+    """--mode prefill --only: config 4's shapes by rows x columns, any other shape as rows x columns (Q4 unless qN
+    follows), nothing for a malformed name."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench.prefill_shapes("") == bench.PREFILL_SHAPES
+    assert bench.prefill_shapes("4864x896") == [(896, 4864, 4)]
+    assert bench.prefill_shapes("65536x896") == [(896, 65536, 8)]
+    assert bench.prefill_shapes("8192x8192") == [(8192, 8192, 4)]
+    assert bench.prefill_shapes("1000x896q8") == [(896, 1000, 8)]
+    assert bench.prefill_shapes("banana") == []
