@@ -39,6 +39,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "../../include/matvec_b200.h"
@@ -539,6 +541,39 @@ static bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// CTAs of `kernel` (kThreads threads, smem bytes of dynamic shared memory, cols TMEM columns) that one SM holds, from
+// its registers, its shared memory and its tensor-memory columns, times the SMs. (The runtime's occupancy query
+// answers one CTA per SM for the 16-token tiles that hold two, as ncu's launch statistics and the waves of a launch
+// show.) Cached per device and kernel.
+static int gemm_slots(const void *kernel, size_t smem, int cols) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void *>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(dev, kernel);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    cudaFuncAttributes fa = {};
+    int sms = 0, regs_sm = 0, smem_sm = 0, reserved = 0, threads_sm = 0;
+    if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) != cudaSuccess || sms <= 0) {
+        cudaGetLastError();
+        return 148;
+    }
+    const int warps = kThreads / 32;
+    const int regs_warp = (fa.numRegs * 32 + 255) / 256 * 256;  // registers are given to a warp 256 at a time
+    int per = regs_warp > 0 ? regs_sm / regs_warp / warps : 1;
+    per = std::min(per, (int)(smem_sm / (smem + fa.sharedSizeBytes + reserved)));
+    per = std::min(per, threads_sm / kThreads);
+    per = std::min(per, 512 / cols);
+    return cache[key] = sms * std::max(per, 1);
+}
+
 template <int BN, int BITS>
 static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mx, const GemmParams &p,
                                cudaStream_t s, bool gather) {
@@ -550,14 +585,21 @@ static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, con
     // 896 at 16 tokens: 22.5 against 19.1 us).
     const int tiles = ((p.d + kBM - 1) / kBM) * ((p.m + BN - 1) / BN);
     auto multi = gather ? gemm_kernel<BN, BITS, true, false> : gemm_kernel<BN, BITS, false, false>;
-    const int slots = resident_slots((const void *)multi, smem, kThreads);
+    auto single = gather ? gemm_kernel<BN, BITS, true, true> : gemm_kernel<BN, BITS, false, true>;
+    // both forms may take the shared memory, and prefer the largest shared-memory carveout
+    cudaError_t e = cudaSuccess;
+    for (auto k : {multi, single}) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    }
+    if (e != cudaSuccess) return e;
+    const int slots = gemm_slots((const void *)multi, smem, Smem<BN, BITS>::kCols);
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const bool one = tiles <= slots || slots >= 2 * sms;
-    auto kernel = one ? (gather ? gemm_kernel<BN, BITS, true, true> : gemm_kernel<BN, BITS, false, true>) : multi;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    kernel<<<one ? tiles : slots, kThreads, smem, s>>>(ma, mb, mx, p);
+    if (one) single<<<tiles, kThreads, smem, s>>>(ma, mb, mx, p);
+    else multi<<<slots, kThreads, smem, s>>>(ma, mb, mx, p);
     return cudaGetLastError();
 }
 

@@ -60,18 +60,17 @@ int resident_slots(const void *kernel, size_t smem, int threads) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return fallback;
     std::lock_guard<std::mutex> lock(mu);
-    int &slots = cache[std::make_tuple(dev, kernel, smem, threads)];
-    if (!slots) {
-        int sms = 0, per_sm = 0;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
-            sms <= 0 || per_sm <= 0) {
-            cudaGetLastError();
-            return fallback;
-        }
-        slots = sms * per_sm;
+    const auto key = std::make_tuple(dev, kernel, smem, threads);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || sms <= 0 ||
+        per_sm <= 0) {
+        cudaGetLastError();
+        return fallback;  // not cached: a later call (say, once the kernel may take more shared memory) asks again
     }
-    return slots;
+    return cache[key] = sms * per_sm;
 }
 
 // Persistent row layout for d rows of n columns: one CTA per resident slot (at most one per row), each owning a
