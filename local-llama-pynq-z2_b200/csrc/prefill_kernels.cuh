@@ -56,16 +56,27 @@ __global__ void embed_rows_kernel(const int8_t *emb_q, const uint16_t *emb_s, co
         x[(size_t)t * dim + i] = __fmul_rn(__int2float_rn(emb_q[r + i]), scale_from_f16(emb_s[r / 32 + i / 32]));
 }
 
-// rmsnorm (qwen.c:337-344) of row t of x with weight w, then quantize: decode_matvec_kernel's kProNorm prologue.
-// Dynamic shared memory: 2n floats.
-__global__ void __launch_bounds__(kThreads) norm_quant_rows_kernel(const float *x, const float *w, float eps, int n,
-                                                                   int8_t *xq, float *xs, int ldx) {
+// rmsnorm (qwen.c:337-344) of row t of x with weight w, then quantize: decode_matvec_kernel's kProNorm prologue;
+// with `add`, row t of add is first added into x (the residual of the matmul before). Dynamic shared memory: 2n
+// floats.
+__global__ void __launch_bounds__(kThreads) norm_quant_rows_kernel(float *x, const float *add, const float *w,
+                                                                   float eps, int n, int8_t *xq, float *xs, int ldx) {
     extern __shared__ __align__(16) float sm[];
     float *xv = sm, *xn = sm + n;
     __shared__ float s_inv;
     const int t = blockIdx.x;
-    const float *xr = x + (size_t)t * n;
-    for (int j = threadIdx.x; j < n / 4; j += kThreads) reinterpret_cast<float4 *>(xv)[j] = ld_cg4(xr + 4 * j);
+    float *xr = x + (size_t)t * n;
+    // with `add`, the residual add of the matmul just before (qwen.c:551, :565) comes first: x += add, stored back
+    const float *ar = add ? add + (size_t)t * n : nullptr;
+    for (int j = threadIdx.x; j < n / 4; j += kThreads) {
+        float4 f = ld_cg4(xr + 4 * j);
+        if (ar) {
+            const float4 a = ld_cg4(ar + 4 * j);
+            f = make_float4(__fadd_rn(f.x, a.x), __fadd_rn(f.y, a.y), __fadd_rn(f.z, a.z), __fadd_rn(f.w, a.w));
+            reinterpret_cast<float4 *>(xr)[j] = f;
+        }
+        reinterpret_cast<float4 *>(xv)[j] = f;
+    }
     __syncthreads();
     for (int j = threadIdx.x; j < n; j += kThreads) xn[j] = __fmul_rn(xv[j], xv[j]);
     __syncthreads();

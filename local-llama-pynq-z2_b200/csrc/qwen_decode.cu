@@ -163,6 +163,10 @@ struct Model {
         float *x = nullptr, *qkv = nullptr, *qb = nullptr, *att = nullptr, *out = nullptr, *h1 = nullptr,
               *h3 = nullptr, *xs = nullptr;
         int8_t *xq = nullptr;
+        // matmuls of one input run side by side (q, k, v; gate, up): two more streams, forked from and joined to
+        // the model's stream by events
+        cudaStream_t side[2] = {nullptr, nullptr};
+        cudaEvent_t fork = nullptr, join[2] = {nullptr, nullptr};
     } pf;
 };
 
@@ -397,6 +401,11 @@ static void destroy(Model *m) {
                     m->pf.out, m->pf.h1, m->pf.h3, m->pf.xs, m->pf.xq};
     for (void *b : bufs)
         if (b) cudaFree(b);
+    for (int i = 0; i < 2; i++) {
+        if (m->pf.side[i]) cudaStreamDestroy(m->pf.side[i]);
+        if (m->pf.join[i]) cudaEventDestroy(m->pf.join[i]);
+    }
+    if (m->pf.fork) cudaEventDestroy(m->pf.fork);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -452,7 +461,12 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
             (e = cudaMalloc(&b.xs, (size_t)(nmax / 32) * ldx * 4)) != cudaSuccess ||
             (e = cudaMalloc(&b.xq, (size_t)cap * nmax)) != cudaSuccess ||
             (e = cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attention_rows_smem_bytes<64>(kMaxCtx, kVChunk))) != cudaSuccess) {
+                                      (int)attention_rows_smem_bytes<64>(kMaxCtx, kVChunk))) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&b.side[0], cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&b.side[1], cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&b.join[0], cudaEventDisableTiming)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&b.join[1], cudaEventDisableTiming)) != cudaSuccess) {
             set_error("mvb_qwen_prefill: batch buffers: %s", cudaGetErrorString(e));
             return -1;
         }
@@ -464,16 +478,29 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
     }
     const cudaStream_t s = m.stream;
     const int ldx = (count + 3) / 4 * 4, T = kThreads;
-    auto gemm = [&](const Mat &w, int n, int d, float *out, int ldo) {
-        return gemm_launch(w.w, w.s, b.xq, b.xs, out, n, d, count, ldx, ldo, 4, s);
+    auto gemm = [&](const Mat &w, int n, int d, float *out, int ldo, cudaStream_t st) {
+        return gemm_launch(w.w, w.s, b.xq, b.xs, out, n, d, count, ldx, ldo, 4, st);
+    };
+    // the side streams start after everything queued on the model's stream so far (fork) and the model's stream
+    // goes on after both (join): matmuls of the same input, writing disjoint outputs, run side by side
+    auto fork = [&]() {
+        return cudaEventRecord(b.fork, s) != cudaSuccess || cudaStreamWaitEvent(b.side[0], b.fork, 0) != cudaSuccess ||
+               cudaStreamWaitEvent(b.side[1], b.fork, 0) != cudaSuccess;
+    };
+    auto join = [&]() {
+        for (int i = 0; i < 2; i++)
+            if (cudaEventRecord(b.join[i], b.side[i]) != cudaSuccess || cudaStreamWaitEvent(s, b.join[i], 0) != cudaSuccess)
+                return true;
+        return false;
     };
     embed_rows_kernel<<<count, T, 0, s>>>((const int8_t *)m.emb.w, (const uint16_t *)m.emb.s, tokens, b.x, dim);
     for (int l = 0; l < L; l++) {
-        norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, m.attn_norm + (size_t)l * dim, c.rms_eps, dim, b.xq,
-                                                             b.xs, ldx);
+        // the previous layer's down residual (x += its matmul output) is folded into this norm
+        norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, l > 0 ? b.out : nullptr, m.attn_norm + (size_t)l * dim,
+                                                             c.rms_eps, dim, b.xq, b.xs, ldx);
         const int ldq = dim + 2 * kv;
-        if (gemm(m.wq[l], dim, dim, b.qkv, ldq) || gemm(m.wk[l], dim, kv, b.qkv + dim, ldq) ||
-            gemm(m.wv[l], dim, kv, b.qkv + dim + kv, ldq))
+        if (fork() || gemm(m.wq[l], dim, dim, b.qkv, ldq, s) || gemm(m.wk[l], dim, kv, b.qkv + dim, ldq, b.side[0]) ||
+            gemm(m.wv[l], dim, kv, b.qkv + dim + kv, ldq, b.side[1]) || join())
             return -1;
         rope_cache_rows_kernel<<<count, T, 0, s>>>(b.qkv, ldq, m.bq + (size_t)l * dim, m.bk + (size_t)l * kv,
                                                    m.bv + (size_t)l * kv, m.rope, m.kcache + (size_t)l * m.ctx * kv,
@@ -484,15 +511,18 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
             b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
             c.n_heads / c.n_kv_heads, npos, vchunk, m.et);
         quant_rows_kernel<<<count, T, dim * 4, s>>>(b.att, dim, b.xq, b.xs, ldx);
-        if (gemm(m.wo[l], dim, dim, b.out, dim)) return -1;
-        residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
-        norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, m.ffn_norm + (size_t)l * dim, c.rms_eps, dim, b.xq,
-                                                             b.xs, ldx);
-        if (gemm(m.w1[l], dim, hid, b.h1, hid) || gemm(m.w3[l], dim, hid, b.h3, hid)) return -1;
+        if (gemm(m.wo[l], dim, dim, b.out, dim, s)) return -1;
+        // x += the o matmul's output, then the FFN norm, in one kernel
+        norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, b.out, m.ffn_norm + (size_t)l * dim, c.rms_eps, dim,
+                                                             b.xq, b.xs, ldx);
+        if (fork() || gemm(m.w1[l], dim, hid, b.h1, hid, s) || gemm(m.w3[l], dim, hid, b.h3, hid, b.side[0]) ||
+            join())
+            return -1;
         swiglu_quant_rows_kernel<<<dim3(count, (hid / 32 + 31) / 32), T, 0, s>>>(b.h1, b.h3, hid, m.et, b.xq, b.xs,
                                                                                  ldx);
-        if (gemm(m.w2[l], hid, dim, b.out, dim)) return -1;
-        residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
+        if (gemm(m.w2[l], hid, dim, b.out, dim, s)) return -1;
+        // x += the down matmul's output: here after the last layer, else in the next layer's first norm
+        if (l == L - 1) residual_rows_kernel<<<(count * dim + T - 1) / T, T, 0, s>>>(b.x, b.out, (size_t)count * dim);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) {
         set_error("mvb_qwen_prefill: launch failed: %s", cudaGetErrorString(e));
