@@ -14,21 +14,23 @@
 // CTA walks tiles blockIdx.x, + gridDim.x, ... (row tiles fastest) with one running k-block count, so the ring, the
 // tensor-memory slots and their barrier phases carry on from one tile into the next: the next tile's copies and
 // MMAs run under this tile's epilogue, and the per-CTA setup and teardown happen once. Otherwise one CTA per tile.
-// Warp roles (320 threads):
+// Warp roles (320 threads; 448 for int4 weights):
 //   warp 0   TMA producer (one thread): per k-block the weight tile (int8, or packed int4), the token tile
 //            (both 128-byte swizzled, the layout the MMA descriptors describe) and the tokens' scales of the
 //            block's four groups ([4][BN] fp32) into the next stage.
 //   warp 1   allocates tensor memory; one thread issues the MMAs: per k-block, D[slot][k] = A_k x B_k^T for its
 //            four groups into one of kSlots TMEM slots (4 for BN <= 32, else 2) of four BN-column group buffers,
 //            then one commit. MMAs run asynchronously, up to kSlots - 1 k-blocks ahead of the epilogue.
-//   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. For
-//            int4 weights they first unpack the packed tile of the k-block kStages/2 ahead into its int8
-//            operand tile (same swizzle), four 16-byte chunks per thread. Per k-block: tcgen05.ld of the
-//            groups' int32 sums, release the slot and the stage, then per group and column
+//   warps 2-9  epilogue: two warps per TMEM lane quadrant (row = lane), each owning BN/2 token columns. Per
+//            k-block: tcgen05.ld of the groups' int32 sums, release the slot and the stage, then per group and column
 //            acc += fl(fl((float)isum * ws) * xs). (float)isum * ws is one fma on a biased integer: with
 //            v = bits(isum + 0x4B400000) = 12582912 + isum (exact for |isum| < 2^22), fma(v, ws, -12582912 * ws)
 //            rounds (v - 12582912) * ws = isum * ws once, and -12582912 * ws is exact because ws has at most 11
 //            significant bits (an fp16 value).
+//   warps 10-13  int4 weights only: unpack each stage's packed tile into its int8 operand tile (same swizzle) as
+//            soon as its copies land, eight 16-byte chunks per thread, for the MMA. Done by the epilogue warps,
+//            the unpack sits on their per-k-block path: 896 x 4864 at 128 tokens takes 41.4 us that way, 31.9 us
+//            with these warps.
 // The token tile BN (16, 32 or 64) is the largest that keeps row tiles x token tiles at half the SM count or more:
 // the in-order sum over groups rules out splitting K across CTAs.
 // Every mbarrier wait is bounded (kGemmWaitNs of %globaltimer); a wait that runs out records an error, the
@@ -52,8 +54,11 @@ namespace gemm {
 
 constexpr int kBM = 128;          // weight rows per CTA (MMA M)
 constexpr int kBK = 128;          // int8 K bytes per stage (4 groups)
-constexpr int kThreads = 320;
+constexpr int kThreads = 320;   // producer, MMA and 8 epilogue warps
 constexpr int kEpiWarps = 8;
+constexpr int kUnpackWarps = 4;  // int4 weights: 4 more warps unpack each stage's packed tile
+template <int BITS>
+constexpr int threads_of() { return BITS == 4 ? kThreads + kUnpackWarps * 32 : kThreads; }
 constexpr unsigned long long kGemmWaitNs = 1000000000ull;
 
 // error codes in the error word (first failure wins)
@@ -212,7 +217,8 @@ struct Smem {
     static constexpr int kRaw = BITS == 4 ? kBM * kBK / 2 : 0;  // packed int4 tile
     static constexpr int kX = 4 * BN * 4;                       // token scales
     static constexpr int kStage = (kA + kB + kRaw + kX + 1023) / 1024 * 1024;
-    // four stages (measured: six to eight, which fit in shared memory, were slower: fewer resident CTAs)
+    // four stages (measured: six to eight, which fit in shared memory, were slower: fewer resident CTAs; for int4
+    // weights, one 448-thread CTA per SM, six to eight were no faster)
     static constexpr int kStages = 4;
     static constexpr size_t kNatural = (size_t)kStages * kStage + 1024 /* align */ + 256 /* barriers */;
     // TMEM: kSlots k-block slots of four group buffers of BN columns (four slots where they fit, so the MMAs can
@@ -243,18 +249,17 @@ __device__ __forceinline__ void unpack_tile(const uint8_t *raw, uint8_t *a, int 
 
 // ONE: every CTA has exactly one tile (the grid is the tile count, within one wave), so the tile loops fold away.
 template <int BN, int BITS, bool GATHER, bool ONE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_of<BITS>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_x, const GemmParams p) {
     using S = Smem<BN, BITS>;
     constexpr int kStages = S::kStages;
-    constexpr int kLag = kStages / 2;  // k-blocks the epilogue warps unpack ahead of the one they finish (int4)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // aligned to 1024 bytes by an offset added to the shared array itself: a pointer that went through an integer
     // cast would be generic, and every stage access through it a generic load or store
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * S::kStage);
-    // full: the stage's copies landed. ready: its int4 tile is unpacked (8 epilogue warps). empty: the epilogue
+    // full: the stage's copies landed. ready: its int4 tile is unpacked (4 unpack warps). empty: the epilogue
     // has finished the stage's k-block (8 warps; its MMAs had completed before that). tfull / tempty: a TMEM
     // k-block slot was written (one commit) / has been read (8 warps).
     constexpr int kSlots = S::kSlots;
@@ -271,13 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nrow = (p.d + kBM - 1) / kBM;
     const int ntiles = nrow * ((p.m + BN - 1) / BN);
     const int mine = ONE ? 1 : ntiles > (int)blockIdx.x ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int total = mine * nkb;  // k-blocks this CTA walks; j below runs over them, tile after tile
     auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&ready[s], kEpiWarps);
+            mbar_init(&ready[s], kUnpackWarps);
             mbar_init(&empty[s], kEpiWarps);
         }
         for (int j = 0; j < kSlots; j++) {
@@ -357,26 +361,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             // all MMAs complete before tensor memory is freed: wait (bounded) for the last commit
             if (j > 0) mbar_wait(&tfull[(j - 1) % kSlots], ((j - 1) / kSlots) & 1, kErrTmemFull);
         }
-    } else {
-        // ---------------- epilogue (and int4 unpack, kLag k-blocks ahead) ----------------
+    } else if (warp < 2 + kEpiWarps) {
+        // ---------------- epilogue ----------------
         constexpr int kCw = BN / 2;               // columns per thread
         constexpr int kLd = kCw < 32 ? kCw : 32;  // columns per TMEM load
         const int q = warp & 3, half = (warp - 2) >> 2;
         const int col0 = half * kCw;
-        const int et = threadIdx.x - 64;  // 0 .. 255
         // this rank's completed calls: the output buffer of this call (parity) in every rank's gather
         const unsigned call = GATHER ? *p.peers.calls : 0u;
         bool ok = true;
-        auto unpack = [&](int j) -> bool {  // unpack k-block j of this CTA's sequence (int4), all 8 warps
-            const int s = j % kStages;
-            if (!mbar_wait(&full[s], (j / kStages) & 1, kErrRaw)) return false;
-            unpack_tile(stage_raw(s), stage_a(s), et, 256);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ready[s]);
-            return true;
-        };
-        if (BITS == 4)
-            for (int j = 0; j < kLag && j < total && ok; j++) ok = unpack(j);
         // this thread's row of tile i, and its weight scales (row 0's past the last row)
         auto row_of = [&](int i) { return (tile_of(i) % nrow) * kBM + q * 32 + lane; };
         auto scales_of = [&](int row) { return p.ws + (size_t)(row < p.d ? row : 0) * p.ng; };
@@ -397,7 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint16_t *wsn = i + 1 < mine ? scales_of(row_of(i + 1)) : wsr;
             for (int kb = 0; kb < nkb; kb++, j++) {
                 const int s = j % kStages, slot = j % kSlots;
-                if (BITS == 4 && j + kLag < total && !(ok = unpack(j + kLag))) break;
                 uint16_t wcur[4];
                 const bool last = kb + 1 == nkb;
 #pragma unroll
@@ -470,6 +462,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (GATHER && p.peers.world > 1) fence_acq_rel_gpu();  // this thread's stores, before the CTA is counted
+    } else if (BITS == 4) {
+        // ---------------- int4 unpack warps ----------------
+        // Per k-block, the packed weight tile into its int8 operand tile, for the MMA: off the epilogue warps' path,
+        // as far ahead as the ring holds stages. The stage was refilled only after the epilogue had finished the
+        // k-block before it (whose MMAs had completed).
+        const int ut = threadIdx.x - kThreads;  // 0 .. 127
+        for (int j = 0; j < mine * nkb; j++) {
+            const int s = j % kStages;
+            if (!mbar_wait(&full[s], (j / kStages) & 1, kErrRaw)) break;
+            unpack_tile(stage_raw(s), stage_a(s), ut, kUnpackWarps * 32);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ready[s]);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -541,11 +546,11 @@ static bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// CTAs of `kernel` (kThreads threads, smem bytes of dynamic shared memory, cols TMEM columns) that one SM holds, from
+// CTAs of `kernel` (blocks of `threads`, smem bytes of dynamic shared memory, cols TMEM columns) that one SM holds, from
 // its registers, its shared memory and its tensor-memory columns, times the SMs. (The runtime's occupancy query
 // answers one CTA per SM for the 16-token tiles that hold two, as ncu's launch statistics and the waves of a launch
 // show.) Cached per device and kernel.
-static int gemm_slots(const void *kernel, size_t smem, int cols) {
+static int gemm_slots(const void *kernel, size_t smem, int cols, int threads) {
     static std::mutex mu;
     static std::map<std::pair<int, const void *>, int> cache;
     int dev = 0;
@@ -565,11 +570,11 @@ static int gemm_slots(const void *kernel, size_t smem, int cols) {
         cudaGetLastError();
         return 148;
     }
-    const int warps = kThreads / 32;
+    const int warps = threads / 32;
     const int regs_warp = (fa.numRegs * 32 + 255) / 256 * 256;  // registers are given to a warp 256 at a time
     int per = regs_warp > 0 ? regs_sm / regs_warp / warps : 1;
     per = std::min(per, (int)(smem_sm / (smem + fa.sharedSizeBytes + reserved)));
-    per = std::min(per, threads_sm / kThreads);
+    per = std::min(per, threads_sm / threads);
     per = std::min(per, 512 / cols);
     return cache[key] = sms * std::max(per, 1);
 }
@@ -594,12 +599,12 @@ static cudaError_t launch_gemm(const CUtensorMap &ma, const CUtensorMap &mb, con
             e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     }
     if (e != cudaSuccess) return e;
-    const int slots = gemm_slots((const void *)multi, smem, Smem<BN, BITS>::kCols);
+    const int slots = gemm_slots((const void *)multi, smem, Smem<BN, BITS>::kCols, threads_of<BITS>());
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const bool one = tiles <= slots || slots >= 2 * sms;
-    if (one) single<<<tiles, kThreads, smem, s>>>(ma, mb, mx, p);
-    else multi<<<slots, kThreads, smem, s>>>(ma, mb, mx, p);
+    if (one) single<<<tiles, threads_of<BITS>(), smem, s>>>(ma, mb, mx, p);
+    else multi<<<slots, threads_of<BITS>(), smem, s>>>(ma, mb, mx, p);
     return cudaGetLastError();
 }
 
