@@ -28,7 +28,9 @@
 //            rounds (v - 12582912) * ws = isum * ws once, and -12582912 * ws is exact because ws has at most 11
 //            significant bits (an fp16 value).
 //   warps 10-13  int4 weights only: unpack each stage's packed tile into its int8 operand tile (same swizzle) as
-//            soon as its copies land, eight 16-byte chunks per thread, for the MMA. Done by the epilogue warps,
+//            soon as its copies land, eight 16-byte chunks per thread, for the MMA. The tile holds 16 * v (the
+//            nibble in the high half of its byte), so the group sums are 16 * isum, |16 * isum| <= 16 * 32 * 8 * 128
+//            < 2^22, and the epilogue's fma above takes ws / 16. Done by the epilogue warps,
 //            the unpack sits on their per-k-block path: 896 x 4864 at 128 tokens takes 41.4 us that way, 31.9 us
 //            with these warps.
 // The token tile BN (16, 32 or 64) is the largest that keeps row tiles x token tiles at half the SM count or more:
@@ -162,13 +164,12 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&r)[8]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// int4 nibbles of one 32-bit word (8 elements, element 2i in the low nibble of byte i) -> 8 int8 values as two
-// words in element order. Sign extension per byte: v | ((v & 8) * 0x1E) maps 8..15 to -8..-1 (0xF8..0xFF) without
-// carries between bytes.
-__device__ __forceinline__ uint2 unpack_int4(uint32_t w) {
-    uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-    lo |= (lo & 0x08080808u) * 0x1Eu;
-    hi |= (hi & 0x08080808u) * 0x1Eu;
+// int4 nibbles of one 32-bit word (8 two's complement elements v, element 2i in the low nibble of byte i) -> the
+// 8 int8 values 16 * v as two words in element order: a nibble moved into the high half of its byte is the int8
+// 16 * v, sign included (two logic operations and two byte permutes per word, no sign extension). The MMA's group
+// sums are then 16 * isum, and the epilogue's weight scale ws / 16.
+__device__ __forceinline__ uint2 unpack_int4_x16(uint32_t w) {
+    const uint32_t lo = (w << 4) & 0xF0F0F0F0u, hi = w & 0xF0F0F0F0u;
     return make_uint2(__byte_perm(lo, hi, 0x5140), __byte_perm(lo, hi, 0x7362));
 }
 
@@ -233,16 +234,20 @@ struct Smem {
 
 // Unpacks the packed int4 tile of a stage ([128 rows][64 bytes]) into its int8 operand tile ([128 rows][128 bytes],
 // 16-byte chunk c of row r stored at chunk c ^ (r & 7): the 128-byte swizzle the TMA applies to the int8 tiles).
-// Shared by the nthreads threads of the calling warps (thread index i); ends with the proxy fence that makes the
-// generic-proxy writes visible to the MMA.
-__device__ __forceinline__ void unpack_tile(const uint8_t *raw, uint8_t *a, int i, int nthreads) {
-#pragma unroll 4
-    for (int u = i; u < kBM * 8; u += nthreads) {
-        const int r = u >> 3, c = u & 7;
-        const uint2 pk = *reinterpret_cast<const uint2 *>(raw + r * (kBK / 2) + c * 8);
-        const uint2 e0 = unpack_int4(pk.x), e1 = unpack_int4(pk.y);
-        *reinterpret_cast<uint4 *>(a + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
-            make_uint4(e0.x, e0.y, e1.x, e1.y);
+// Values 16 * v (unpack_int4_x16). Shared by the NT threads of the calling warps (thread index i): thread i does
+// chunk i & 7 of rows i / 8, + NT / 8, ... (NT / 8 is a multiple of 8, so the swizzled chunk stays the thread's).
+// Ends with the proxy fence that makes the generic-proxy writes visible to the MMA.
+template <int NT>
+__device__ __forceinline__ void unpack_tile(const uint8_t *raw, uint8_t *a, int i) {
+    static_assert(NT % 64 == 0 && (kBM * 8) % NT == 0, "whole passes of rows in steps of 8");
+    const int r = i >> 3, c = i & 7;
+    const uint8_t *src = raw + r * (kBK / 2) + c * 8;
+    uint8_t *dst = a + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
+#pragma unroll
+    for (int k = 0; k < kBM * 8 / NT; k++) {
+        const uint2 pk = *reinterpret_cast<const uint2 *>(src + k * (NT / 8) * (kBK / 2));
+        const uint2 e0 = unpack_int4_x16(pk.x), e1 = unpack_int4_x16(pk.y);
+        *reinterpret_cast<uint4 *>(dst + k * (NT / 64) * 1024) = make_uint4(e0.x, e0.y, e1.x, e1.y);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -421,7 +426,8 @@ __global__ void __launch_bounds__(threads_of<BITS>(), 1)
                     for (int g = 0; g < kG; g++) {
                         const int k = k0 + g;
                         if (k >= ng_kb) break;
-                        const float wsc = scale_from_f16(wcur[k]);
+                        // int4 tiles hold 16 * v: their sums are 16 * isum, and ws / 16 is exact (a power of two)
+                        const float wsc = BITS == 4 ? __fmul_rn(scale_from_f16(wcur[k]), 0.0625f) : scale_from_f16(wcur[k]);
                         const float ncw = __fmul_rn(-12582912.0f, wsc);  // exact: wsc has <= 11 significant bits
                         const float *xsg = xst + k * BN + col0;
 #pragma unroll
@@ -471,7 +477,7 @@ __global__ void __launch_bounds__(threads_of<BITS>(), 1)
         for (int j = 0; j < mine * nkb; j++) {
             const int s = j % kStages;
             if (!mbar_wait(&full[s], (j / kStages) & 1, kErrRaw)) break;
-            unpack_tile(stage_raw(s), stage_a(s), ut, kUnpackWarps * 32);
+            unpack_tile<kUnpackWarps * 32>(stage_raw(s), stage_a(s), ut);
             __syncwarp();
             if (lane == 0) mbar_arrive(&ready[s]);
         }
