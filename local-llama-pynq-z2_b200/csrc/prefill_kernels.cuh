@@ -238,5 +238,95 @@ inline size_t attention_rows_smem_bytes(int npos, int vchunk) {
     return (size_t)HS * 4 + (size_t)((npos + 3) & ~3) * 4 + (size_t)vchunk * HS * 4;
 }
 
+// The same causal attention (qwen.c:521-546) with the keys and values shared by the query heads of a group: one CTA
+// per (token t,
+// kv head) and one warp per query head of the group (kv_mul warps). The kv head's keys and values of positions
+// 0 .. pos are staged into shared memory once (16-byte cp.async pieces) and read by every warp, where
+// attention_rows_kernel has each of the kv_mul query-head CTAs read them from L2 on its own. Per query head the
+// arithmetic is attention_rows_kernel's, operation for operation, so the outputs are the same bits:
+//   scores   s_u = ((0 + q_0 k_u0) + q_1 k_u1) + ... in dimension order, then s_u / sqrt(HS)   (lane: u = lane + 32i,
+//            four positions at a time)
+//   softmax  max (order-free), expf_ref(s_u - max), the sum in position order (lane 0), then s_u / sum
+//   values   out_d = ((0 + a_0 v_0d) + a_1 v_1d) + ... + a_pos v_pos,d in position order        (lane: d = lane + 32j)
+// The key rows are padded to HS + 4 floats: the float4 reads of eight consecutive lanes (eight consecutive rows)
+// then fall in eight different 16-byte bank groups. Shared memory: attention_gqa_smem_bytes(npos, kv_mul).
+template <int HS>
+__global__ void __launch_bounds__(1024) attention_gqa_rows_kernel(const float *qb, const float *kcache,
+                                                                   const float *vcache, float *out, int p0, int dim,
+                                                                   int kv_dim, int kv_mul, int npos, ExpTable et) {
+    static_assert(HS % 32 == 0, "whole lanes per head dimension");
+    constexpr int KS = HS + 4;
+    extern __shared__ __align__(16) float gsm[];
+    const int t = blockIdx.x, kvh = blockIdx.y, pos = p0 + t, tid = threadIdx.x;
+    const int npad = (npos + 3) & ~3;
+    float *ks = gsm;                          // [npos][KS] keys
+    float *vs = ks + (size_t)npos * KS;       // [npos][HS] values
+    float *att = vs + (size_t)npos * HS;      // [kv_mul][npad] scores, then weights
+    float *qs = att + (size_t)kv_mul * npad;  // [kv_mul][HS] the group's queries
+    for (int c = tid; c < (pos + 1) * (HS / 4); c += blockDim.x) {
+        const int u = c / (HS / 4), k = c % (HS / 4);
+        const size_t g = (size_t)u * kv_dim + kvh * HS + 4 * k;
+        cp_async16(ks + u * KS + 4 * k, kcache + g);
+        cp_async16(vs + u * HS + 4 * k, vcache + g);
+    }
+    cp_async_commit();
+    for (int c = tid; c < kv_mul * HS; c += blockDim.x) qs[c] = qb[(size_t)t * dim + (size_t)kvh * kv_mul * HS + c];
+    cp_async_wait<0>();
+    __syncthreads();
+    const int w = tid >> 5, lane = tid & 31, h = kvh * kv_mul + w;
+    const float *q = qs + w * HS;
+    float *a = att + w * npad;
+    const float scale = __fsqrt_rn((float)HS);
+    float m = -INFINITY;
+    for (int u0 = 0; u0 <= pos; u0 += 128) {
+        int row[4];
+        float sc[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int u = u0 + 32 * r + lane;
+            row[r] = u <= pos ? u : 0;  // past pos: row 0 (staged), result unused
+            sc[r] = 0.0f;
+        }
+#pragma unroll 4
+        for (int i = 0; i < HS; i += 4) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(q + i);
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const float4 k4 = *reinterpret_cast<const float4 *>(ks + row[r] * KS + i);
+                sc[r] = __fadd_rn(sc[r], __fmul_rn(q4.x, k4.x));
+                sc[r] = __fadd_rn(sc[r], __fmul_rn(q4.y, k4.y));
+                sc[r] = __fadd_rn(sc[r], __fmul_rn(q4.z, k4.z));
+                sc[r] = __fadd_rn(sc[r], __fmul_rn(q4.w, k4.w));
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int u = u0 + 32 * r + lane;
+            if (u <= pos) {
+                const float v = __fdiv_rn(sc[r], scale);
+                a[u] = v;
+                m = fmaxf(m, v);
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    for (int u = lane; u <= pos; u += 32) a[u] = expf_ref(__fsub_rn(a[u], m), et);
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0) sum = chain_sum(a, pos + 1);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int u = lane; u <= pos; u += 32) a[u] = __fdiv_rn(a[u], sum);
+    __syncwarp();
+#pragma unroll
+    for (int d = lane; d < HS; d += 32) out[(size_t)t * dim + h * HS + d] = weighted_chain<HS>(0.0f, a, vs + d, pos + 1);
+}
+
+// Shared memory of attention_gqa_rows_kernel for positions 0 .. npos-1 and kv_mul query heads per kv head.
+template <int HS>
+inline size_t attention_gqa_smem_bytes(int npos, int kv_mul) {
+    return (size_t)npos * (2 * HS + 4) * 4 + (size_t)kv_mul * (((npos + 3) & ~3) + HS) * 4;
+}
+
 }  // namespace decode
 }  // namespace mvb

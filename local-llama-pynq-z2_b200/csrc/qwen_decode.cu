@@ -440,6 +440,7 @@ static int wait_stream(Model &m, const char *who, double budget_s) {
 }
 
 constexpr int kBatchCap = 256;  // prompt tokens per batched prefill pass
+constexpr int kGqaSmemMax = 200 * 1024;  // shared memory of the grouped prefill attention, at most
 
 // Runs prompt tokens tokens[0 .. count-1] (device) at positions p0 .. p0+count-1 through every layer as one batch
 // (no head: qwen.c discards the logits of prompt positions), writing their KV-cache rows exactly as the decode
@@ -462,6 +463,8 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
             (e = cudaMalloc(&b.xq, (size_t)cap * nmax)) != cudaSuccess ||
             (e = cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)attention_rows_smem_bytes<64>(kMaxCtx, kVChunk))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(attention_gqa_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kGqaSmemMax)) != cudaSuccess ||
             (e = cudaStreamCreateWithFlags(&b.side[0], cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaStreamCreateWithFlags(&b.side[1], cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming)) != cudaSuccess ||
@@ -505,11 +508,21 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
         rope_cache_rows_kernel<<<count, T, 0, s>>>(b.qkv, ldq, m.bq + (size_t)l * dim, m.bk + (size_t)l * kv,
                                                    m.bv + (size_t)l * kv, m.rope, m.kcache + (size_t)l * m.ctx * kv,
                                                    m.vcache + (size_t)l * m.ctx * kv, b.qb, p0, dim, kv, m.hs);
-        // shared memory for the positions this batch reaches only: more CTAs per SM
-        const int npos = p0 + count, vchunk = npos < kVChunk ? (npos + 7) / 8 * 8 : kVChunk;
-        attention_rows_kernel<64><<<dim3(count, c.n_heads), T, attention_rows_smem_bytes<64>(npos, vchunk), s>>>(
-            b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
-            c.n_heads / c.n_kv_heads, npos, vchunk, m.et);
+        // shared memory for the positions this batch reaches only: more CTAs per SM. Where the kv head's keys and
+        // values of every position fit in one CTA's shared memory, one CTA per (token, kv head) stages them once
+        // for the group's query heads; otherwise one CTA per (token, query head) reads them in chunks.
+        const int npos = p0 + count, kv_mul = c.n_heads / c.n_kv_heads;
+        const size_t gqa_smem = attention_gqa_smem_bytes<64>(npos, kv_mul);
+        if (gqa_smem <= (size_t)kGqaSmemMax && kv_mul * 32 <= 1024) {
+            attention_gqa_rows_kernel<64><<<dim3(count, c.n_kv_heads), kv_mul * 32, gqa_smem, s>>>(
+                b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
+                kv_mul, npos, m.et);
+        } else {
+            const int vchunk = npos < kVChunk ? (npos + 7) / 8 * 8 : kVChunk;
+            attention_rows_kernel<64><<<dim3(count, c.n_heads), T, attention_rows_smem_bytes<64>(npos, vchunk), s>>>(
+                b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
+                kv_mul, npos, vchunk, m.et);
+        }
         quant_rows_kernel<<<count, T, dim * 4, s>>>(b.att, dim, b.xq, b.xs, ldx);
         if (gemm(m.wo[l], dim, dim, b.out, dim, s)) return -1;
         // x += the o matmul's output, then the FFN norm, in one kernel
