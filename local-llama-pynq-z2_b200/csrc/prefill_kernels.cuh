@@ -238,6 +238,44 @@ inline size_t attention_rows_smem_bytes(int npos, int vchunk) {
     return (size_t)HS * 4 + (size_t)((npos + 3) & ~3) * 4 + (size_t)vchunk * HS * 4;
 }
 
+// acc_lo = ((0 + a_0 v_0) + a_1 v_1) + ... over t < nt in order, and acc_hi the same for the value beside it: two
+// independent in-order chains (values at vb + t * HS and vb + t * HS + 1; vb 8-byte aligned, a 16-byte aligned).
+// The products of a block of 8 positions are formed one block ahead of their adds.
+template <int HS>
+__device__ __forceinline__ float2 weighted_chain_pair(const float *a, const float *vb, int nt) {
+    float2 acc = make_float2(0.0f, 0.0f);
+    const int n8 = nt & ~7;
+    auto form = [&](int t0, float2 (&p)[8]) {
+        const float4 a0 = *reinterpret_cast<const float4 *>(a + t0), a1 = *reinterpret_cast<const float4 *>(a + t0 + 4);
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float2 v = *reinterpret_cast<const float2 *>(vb + (t0 + i) * HS);
+            p[i] = make_float2(__fmul_rn(av[i], v.x), __fmul_rn(av[i], v.y));
+        }
+    };
+    float2 p[8];
+    if (n8 > 0) form(0, p);
+    for (int t = 0; t < n8; t += 8) {
+        float2 nx[8];
+        form(t + 8 < n8 ? t + 8 : t, nx);  // stays inside [0, n8)
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            acc.x = __fadd_rn(acc.x, p[i].x);
+            acc.y = __fadd_rn(acc.y, p[i].y);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) p[i] = nx[i];
+    }
+    for (int t = n8; t < nt; t++) {
+        const float av = a[t];
+        const float2 v = *reinterpret_cast<const float2 *>(vb + t * HS);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(av, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(av, v.y));
+    }
+    return acc;
+}
+
 // The same causal attention (qwen.c:521-546) with the keys and values shared by the query heads of a group: one CTA
 // per (token t,
 // kv head) and one warp per query head of the group (kv_mul warps). The kv head's keys and values of positions
@@ -247,14 +285,18 @@ inline size_t attention_rows_smem_bytes(int npos, int vchunk) {
 //   scores   s_u = ((0 + q_0 k_u0) + q_1 k_u1) + ... in dimension order, then s_u / sqrt(HS)   (lane: u = lane + 32i,
 //            four positions at a time)
 //   softmax  max (order-free), expf_ref(s_u - max), the sum in position order (lane 0), then s_u / sum
-//   values   out_d = ((0 + a_0 v_0d) + a_1 v_1d) + ... + a_pos v_pos,d in position order        (lane: d = lane + 32j)
-// The key rows are padded to HS + 4 floats: the float4 reads of eight consecutive lanes (eight consecutive rows)
-// then fall in eight different 16-byte bank groups. Shared memory: attention_gqa_smem_bytes(npos, kv_mul).
+//   values   o_d = ((0 + a_0 v_0d) + a_1 v_1d) + ... + a_pos v_pos,d in position order     (lane: d = 2 lane, 2 lane + 1)
+// and then, in place of quant_rows_kernel, the quantization of the head's 64 outputs for the o projection: they are
+// whole groups of 32 (lanes 0-15 and 16-31), quantized with quantize_row's operations (qwen.c:355-364) into xq
+// (token-major) and xs (group-major, ldx). The key rows are padded to HS + 4 floats: the float4 reads of eight
+// consecutive lanes (eight consecutive rows) then fall in eight different 16-byte bank groups. Shared memory:
+// attention_gqa_smem_bytes(npos, kv_mul).
 template <int HS>
 __global__ void __launch_bounds__(1024) attention_gqa_rows_kernel(const float *qb, const float *kcache,
-                                                                   const float *vcache, float *out, int p0, int dim,
-                                                                   int kv_dim, int kv_mul, int npos, ExpTable et) {
-    static_assert(HS % 32 == 0, "whole lanes per head dimension");
+                                                                   const float *vcache, int8_t *xq, float *xs, int ldx,
+                                                                   int p0, int dim, int kv_dim, int kv_mul, int npos,
+                                                                   ExpTable et) {
+    static_assert(HS == 64, "two values per lane, two quantization groups per head");
     constexpr int KS = HS + 4;
     extern __shared__ __align__(16) float gsm[];
     const int t = blockIdx.x, kvh = blockIdx.y, pos = p0 + t, tid = threadIdx.x;
@@ -318,8 +360,21 @@ __global__ void __launch_bounds__(1024) attention_gqa_rows_kernel(const float *q
     sum = __shfl_sync(0xffffffffu, sum, 0);
     for (int u = lane; u <= pos; u += 32) a[u] = __fdiv_rn(a[u], sum);
     __syncwarp();
+    const float2 o = weighted_chain_pair<HS>(a, vs + 2 * lane, pos + 1);
+    // quantize_row's operations on the group of lanes 0-15 (dims 0-31) and of lanes 16-31 (dims 32-63)
+    auto bits = [](float x) {
+        const float v = fabsf(x);
+        return v == v ? __float_as_uint(v) : 0u;
+    };
+    unsigned mb = max(bits(o.x), bits(o.y));
 #pragma unroll
-    for (int d = lane; d < HS; d += 32) out[(size_t)t * dim + h * HS + d] = weighted_chain<HS>(0.0f, a, vs + d, pos + 1);
+    for (int off = 1; off < 16; off <<= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+    const float qscale = __fmul_rn(__uint_as_float(mb), 1.0f / 127.0f);
+    const float inv = qscale > 0.0f ? __frcp_rn(qscale) : 0.0f;
+    const uint32_t q0 = (uint8_t)to_int8_x86(roundf(__fmul_rn(o.x, inv)));
+    const uint32_t q1 = (uint8_t)to_int8_x86(roundf(__fmul_rn(o.y, inv)));
+    *reinterpret_cast<uint16_t *>(xq + (size_t)t * dim + h * HS + 2 * lane) = (uint16_t)(q0 | q1 << 8);
+    if ((lane & 15) == 0) xs[(size_t)(2 * h + (lane >> 4)) * ldx + t] = qscale;
 }
 
 // Shared memory of attention_gqa_rows_kernel for positions 0 .. npos-1 and kv_mul query heads per kv head.

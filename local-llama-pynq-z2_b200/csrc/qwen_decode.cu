@@ -514,16 +514,17 @@ static int prefill_batch(Model &m, const int *tokens, int p0, int count) {
         const int npos = p0 + count, kv_mul = c.n_heads / c.n_kv_heads;
         const size_t gqa_smem = attention_gqa_smem_bytes<64>(npos, kv_mul);
         if (gqa_smem <= (size_t)kGqaSmemMax && kv_mul * 32 <= 1024) {
+            // quantizes its outputs for the o projection itself
             attention_gqa_rows_kernel<64><<<dim3(count, c.n_kv_heads), kv_mul * 32, gqa_smem, s>>>(
-                b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
-                kv_mul, npos, m.et);
+                b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.xq, b.xs, ldx, p0, dim,
+                kv, kv_mul, npos, m.et);
         } else {
             const int vchunk = npos < kVChunk ? (npos + 7) / 8 * 8 : kVChunk;
             attention_rows_kernel<64><<<dim3(count, c.n_heads), T, attention_rows_smem_bytes<64>(npos, vchunk), s>>>(
                 b.qb, m.kcache + (size_t)l * m.ctx * kv, m.vcache + (size_t)l * m.ctx * kv, b.att, p0, dim, kv,
                 kv_mul, npos, vchunk, m.et);
+            quant_rows_kernel<<<count, T, dim * 4, s>>>(b.att, dim, b.xq, b.xs, ldx);
         }
-        quant_rows_kernel<<<count, T, dim * 4, s>>>(b.att, dim, b.xq, b.xs, ldx);
         if (gemm(m.wo[l], dim, dim, b.out, dim, s)) return -1;
         // x += the o matmul's output, then the FFN norm, in one kernel
         norm_quant_rows_kernel<<<count, T, 2 * dim * 4, s>>>(b.x, b.out, m.ffn_norm + (size_t)l * dim, c.rms_eps, dim,
