@@ -94,10 +94,12 @@ def test_prefill_decode_equals_generate(qwen05b):
     assert dec.decode(24).tolist() == whole
 
 
-@pytest.mark.parametrize("n", [1, 2, 37, 129, 300])
+@pytest.mark.parametrize("n", [1, 2, 37, 129, 300, 400])
 def test_batched_prefill_equals_tokenwise(qwen05b, n):
     """The batched prefill (tensor-core matmuls, batched attention; batches of 256, so 300 tokens take two) writes
-    the KV-cache rows of one decode step per token bit for bit, and decoding continues identically."""
+    the KV-cache rows of one decode step per token bit for bit, and decoding continues identically. At 400 tokens
+    the second batch reaches 399 positions, more than the grouped attention stages in shared memory, so it runs the
+    chunked one-CTA-per-query-head attention and the separate quantize."""
     _, dec = qwen05b
     prompt = [int(t) for t in np.random.default_rng(100 + n).integers(0, 151936, n)]
     dec.prefill_tokenwise(prompt)
